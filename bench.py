@@ -1,0 +1,339 @@
+#!/usr/bin/env python3
+"""Benchmark of the hot path: decoder_feedforward (one decode token) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: one token through the NVFP4 GeGLU MLP block of Gemma-4-12B
+(x ~ N(0,1) bf16, RMSNorm weights ~ N(0,0.1), gate/up [15360x3840] and down
+[3840x15360] from N(0,0.02) quantized to NVFP4), seeded synthetic data.  A step is one
+token through one layer's block; steps cycle through 4 layers' distinct weights
+(4 x 99.6 MB > the 126 MB L2), so every step streams its weights from HBM.
+
+N=1: `value` = device time per token (CUDA events on the launching stream).  N>1
+(torchrun): tensor parallel, each rank holds 1/N of every layer (column-parallel
+gate/up, row-parallel down) and the block ends in one all-reduce; `value` = the max over
+ranks of the device time per token ("strong" scaling: the work per token is fixed).
+`e2e` times the same op through the C ABI with the residual copied from pinned host
+memory before and read back after every step.  `--impl reference` times the reference's
+PyTorch CPU path on this host's cores instead (rank 0 only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "furiosa-opt-gemma4-12b_b200"))
+
+METRIC = "decoder_feedforward µs/token"
+UNIT = "µs/token"
+H, L = 3840, 15360
+NLAYERS = 4
+# algorithmic bytes of one token (TP1): NVFP4 codes + E4M3 block scales of gate/up/down,
+# three f32 global scales, residual in/out, two norm weights, layer scalar
+WEIGHT_BYTES = 3 * (L * H // 2) + 3 * (L * H // 16)
+ACT_BYTES = 12 + 2 * H * 2 + 2 * H * 2 + 16
+
+
+def algorithmic_bytes(world: int) -> int:
+    return WEIGHT_BYTES // world + ACT_BYTES
+
+
+def measured_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+def profile_traffic() -> float | None:
+    """dram bytes per launch of the MLP kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "decoder_feedforward_traffic.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["dram_bytes_per_launch"])
+        except Exception:
+            return None
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons with NVML while the timed region runs."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device: int, period_s: float = 0.005):
+        self.samples, self.reasons, self.ok = [], set(), False
+        self.period = period_s
+        self.max_mhz = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.ok = False
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for b, name in self.REASONS.items():
+                    if bits & b and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self) -> dict:
+        s = sorted(self.samples)
+        return {"sm_mhz": s[len(s) // 2] if s else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(s)}
+
+
+def make_layers(device: str, rank: int, world: int):
+    import torch
+    from g4b200 import quant, tp
+
+    layers = []
+    for i in range(NLAYERS):
+        m = quant.mlp_config1(seed=i, device=device)
+        if world > 1:
+            m = tp.shard_mlp(m, rank, world)
+        layers.append(m)
+    torch.cuda.synchronize()
+    return layers
+
+
+def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
+    import torch
+    import torch.distributed as dist
+
+    import g4b200 as g4
+
+    torch.cuda.set_device(local_rank)
+    dev = f"cuda:{local_rank}"
+    stream = torch.cuda.Stream(device=dev)
+    tpinfo = None
+    if world > 1:
+        nid = [g4.Context.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(nid, src=0)
+        tpinfo = (rank, world, nid[0])
+    ctx = g4.Context(local_rank, stream=stream, tp=tpinfo)
+    layers = make_layers(dev, rank, world)
+    residual = layers[0]["residual"].clone()
+
+    def step(i: int) -> None:
+        m = dict(layers[i % NLAYERS])
+        m["residual"] = residual
+        g4.decoder_feedforward(ctx, **m)
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+    stream.synchronize()
+    if ctx.poll() != 0:
+        raise RuntimeError("device status set during warm-up")
+    if not torch.isfinite(residual.float()).all():
+        raise RuntimeError("non-finite residual after warm-up")
+
+    # ---------------------------------------------------------------- device-timed region
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local_rank)
+    with sampler, torch.cuda.stream(stream):
+        t0.record(stream)
+        for i in range(args.steps):
+            evs[i][0].record(stream)
+            step(i)
+            evs[i][1].record(stream)
+        t1.record(stream)
+        stream.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    total_ms = t0.elapsed_time(t1)
+    kernel_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+    status = ctx.poll()
+
+    # ---------------------------------------------------------------- end to end (host buffers)
+    host_in = torch.empty(H, dtype=torch.bfloat16, pin_memory=True)
+    host_in.copy_(layers[0]["residual"].cpu())
+    host_out = torch.empty(H, dtype=torch.bfloat16, pin_memory=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = min(args.steps, 2000)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(e2e_steps):
+            residual.copy_(host_in, non_blocking=True)
+            step(i)
+            host_out.copy_(residual, non_blocking=True)
+            stream.synchronize()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+
+    vals = torch.tensor([total_ms / args.steps, kernel_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms_per_step, kernel_ms, e2e_ms = vals.tolist()
+    ctx.close()
+    if rank != 0:
+        return None
+
+    peak, peak_kind = measured_peaks()
+    achieved = algorithmic_bytes(world) / (kernel_ms * 1e-3) / 1e9
+    traffic = profile_traffic() if world == 1 else None
+    line = {
+        "metric": METRIC, "value": round(ms_per_step * 1000.0, 3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "nvfp4 weights, bf16 act, f32 acc",
+        "data": "synthetic (seeded N(0,1) x, N(0,0.1) norms, N(0,0.02) weights quantized to NVFP4)",
+        "config": {"workload": "decoder_feedforward one token, BASELINE config 1 (H=3840, L=15360, NVFP4)",
+                   "global_batch": 1, "seq_len": 1, "parallelism": f"tp{world}",
+                   "layers_cycled": NLAYERS, "l2": f"inputs larger than L2 ({NLAYERS} layers x "
+                   f"{WEIGHT_BYTES / 1e6:.1f} MB weights cycled per step)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                     "traffic": traffic, "algorithmic_bytes_per_launch": algorithmic_bytes(world),
+                     "kernel_us": round(kernel_ms * 1000.0, 3)},
+        "e2e": {"value": round(e2e_ms * 1000.0, 3), "unit": UNIT, "h2d_bytes_per_step": H * 2,
+                "d2h_bytes_per_step": H * 2},
+        "gpu_launches": args.steps * (1 if world == 1 else 2),
+        "clocks": sampler.summary(),
+        "device_status": status,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.cpu_budget)
+    return line
+
+
+def cpu_baseline(budget_s: float) -> dict:
+    """The reference's PyTorch CPU path (oracle port) on this host, bounded sample."""
+    sys.path.insert(0, str(ROOT))
+    import torch
+
+    from g4b200 import quant
+    from oracle import cpu_reference
+
+    m = quant.mlp_config1(seed=0, device="cpu")
+    ref = cpu_reference.ReferenceFeedforward(m)
+    med, n, threads = cpu_reference.time_tokens(ref, m["residual"], budget_s=budget_s)
+    return {"value": round(med * 1e6, 1), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{n} tokens of decoder_feedforward (config 1, layer 0), median, torch CPU bf16 "
+                      f"GloballyScaled MLP as in scripts/generate_references.py:588-639"}
+
+
+def run_reference(args, rank: int, world: int) -> dict | None:
+    if rank != 0:
+        return None
+    sys.path.insert(0, str(ROOT))
+    import torch
+
+    from g4b200 import quant
+    from oracle import cpu_reference
+
+    m = quant.mlp_config1(seed=0, device="cpu")
+    ref = cpu_reference.ReferenceFeedforward(m)
+    torch.set_num_threads(os.cpu_count() or 1)
+    x = m["residual"]
+    for _ in range(max(1, min(args.warmup, 3))):
+        ref(x)
+    steps = max(1, min(args.steps, args.ref_steps))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        ref(x)
+    dt = (time.perf_counter() - t0) / steps
+    v = round(dt * 1e6, 1)
+    return {
+        "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3, 3), "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16 (dequantised NVFP4 weights), CPU", "data": "synthetic (same as ours)", "impl": "reference",
+        "config": {"workload": "decoder_feedforward one token, BASELINE config 1 (H=3840, L=15360, NVFP4)",
+                   "global_batch": 1, "seq_len": 1, "parallelism": "cpu"},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"{steps} tokens, layer-0 weights, torch CPU GloballyScaled MLP"},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--ref-steps", type=int, default=10)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line:
+            print(json.dumps(line), flush=True)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device(f"cuda:{local_rank}"))
+    try:
+        line = run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+    if line:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,396 @@
+// The C ABI of include/g4.h: argument validation and dispatch to the kernel launchers.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstring>
+#include <string>
+
+#include "g4_internal.h"
+#include "g4_common.cuh"
+
+namespace g4 {
+
+g4_status fail(g4_ctx* ctx, g4_status code, const std::string& msg) {
+  if (ctx) ctx->last_error = msg;
+  return code;
+}
+g4_status check_cuda(g4_ctx* ctx, cudaError_t err, const char* what) {
+  if (err == cudaSuccess) return G4_OK;
+  return fail(ctx, G4_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
+}
+bool aligned16(const void* p) { return p != nullptr && (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// NCCL is resolved at run time, only when tensor parallelism is used: a process that
+// already loaded an NCCL (e.g. torch's bundled one) keeps using that copy, and a
+// single-GPU process never loads one.
+struct NcclApi {
+  bool ok = false;
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+static NcclApi& nccl() {
+  static NcclApi api;
+  static bool tried = false;
+  if (tried) return api;
+  tried = true;
+  void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+  if (h == nullptr) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+  if (h == nullptr) return api;
+  api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+  api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+  api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+  api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+  api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+  api.ok = api.get_unique_id && api.comm_init_rank && api.all_reduce && api.comm_destroy && api.error_string;
+  return api;
+}
+
+g4_status allreduce_f32(g4_ctx* ctx, float* buf, size_t count) {
+  if (ctx->comm == nullptr || !nccl().ok) return fail(ctx, G4_ERR_NCCL, "tensor parallelism without a communicator");
+  const ncclResult_t r =
+      nccl().all_reduce(buf, buf, count, ncclFloat32, ncclSum, reinterpret_cast<ncclComm_t>(ctx->comm), ctx->stream);
+  if (r != ncclSuccess) return fail(ctx, G4_ERR_NCCL, std::string("ncclAllReduce: ") + nccl().error_string(r));
+  return G4_OK;
+}
+
+// launchers (other translation units)
+g4_status launch_qkv(g4_ctx*, bool, bool, const uint16_t*, const uint8_t* const[3], const uint8_t* const[3],
+                     const uint16_t* const[3], const float* const[3], const uint16_t*, const uint16_t*,
+                     const uint16_t*, const int32_t*, const int32_t*, const uint16_t*, const uint16_t*, uint16_t*,
+                     uint16_t*, uint16_t*);
+g4_status launch_oproj(g4_ctx*, bool, bool, const uint16_t*, const float*, const uint16_t*, const uint8_t*,
+                       const uint8_t*, const uint16_t*, const float*, uint16_t*);
+g4_status launch_lm_head(g4_ctx*, const uint16_t*, const uint16_t*, const uint16_t*, uint16_t*);
+g4_status launch_sliding_attention(g4_ctx*, const uint16_t*, const uint16_t*, const uint16_t*, const float*,
+                                   uint16_t*);
+g4_status launch_full_page(g4_ctx*, bool, const uint16_t*, const uint16_t*, const uint16_t*, const float*, float*,
+                           float*, uint16_t*);
+g4_status launch_full_paged(g4_ctx*, const uint16_t*, const uint16_t* const*, const uint16_t* const*, int, int,
+                            float*, uint16_t*);
+g4_status launch_embed(g4_ctx*, const uint16_t*, const int32_t*, uint16_t*);
+g4_status launch_argmax(g4_ctx*, const uint16_t*, int, int32_t*);
+g4_status launch_dequant_nvfp4(g4_ctx*, const uint8_t*, const uint8_t*, int, int, uint16_t*);
+g4_status launch_dequant_fp8(g4_ctx*, const uint8_t*, long long, uint16_t*);
+
+}  // namespace g4
+
+using namespace g4;
+
+#define G4_CHECK_CTX(ctx) \
+  if ((ctx) == nullptr) return G4_ERR_BAD_ARG
+// Every listed pointer must be non-null and 16-byte aligned.
+#define G4_REQUIRE_PTRS(ctx, ...)                                                          \
+  do {                                                                                     \
+    const void* _ptrs[] = {__VA_ARGS__};                                                   \
+    for (size_t _i = 0; _i < sizeof(_ptrs) / sizeof(_ptrs[0]); ++_i)                       \
+      if (!aligned16(_ptrs[_i]))                                                           \
+        return fail(ctx, G4_ERR_BAD_ARG, "argument " + std::to_string(_i) +                \
+                                             " is null or not 16-byte aligned");           \
+  } while (0)
+// Scalars/offsets need only natural alignment.
+#define G4_REQUIRE_SCALARS(ctx, ...)                                                       \
+  do {                                                                                     \
+    const void* _ptrs[] = {__VA_ARGS__};                                                   \
+    for (size_t _i = 0; _i < sizeof(_ptrs) / sizeof(_ptrs[0]); ++_i)                       \
+      if (_ptrs[_i] == nullptr || (reinterpret_cast<uintptr_t>(_ptrs[_i]) & 3u))           \
+        return fail(ctx, G4_ERR_BAD_ARG, "scalar argument " + std::to_string(_i) +         \
+                                             " is null or misaligned");                    \
+  } while (0)
+
+extern "C" {
+
+const char* g4_version(void) { return "g4b200 0.1.0 sm_100a"; }
+
+g4_status g4_ctx_create(int device, g4_ctx** out) {
+  if (out == nullptr) return G4_ERR_BAD_ARG;
+  *out = nullptr;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count) return G4_ERR_CUDA;
+  g4_ctx* ctx = new g4_ctx();
+  ctx->device = device;
+  g4_status st = check_cuda(ctx, cudaSetDevice(device), "cudaSetDevice");
+  if (st == G4_OK)
+    st = check_cuda(ctx, cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device), "sm count");
+  int major = 0;
+  if (st == G4_OK) st = check_cuda(ctx, cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device), "cc");
+  if (st == G4_OK && major != 10) st = fail(ctx, G4_ERR_UNSUPPORTED, "g4b200 needs a compute capability 10.0 GPU");
+  DeviceBuffers& b = ctx->buf;
+  if (st == G4_OK) st = check_cuda(ctx, cudaMalloc(&b.scratch, sizeof(Scratch)), "cudaMalloc scratch");
+  if (st == G4_OK) st = check_cuda(ctx, cudaMemset(b.scratch, 0, sizeof(Scratch)), "cudaMemset scratch");
+  if (st == G4_OK) st = check_cuda(ctx, cudaMalloc(&b.part, kPartFloats * 4), "cudaMalloc part");
+  if (st == G4_OK) st = check_cuda(ctx, cudaMalloc(&b.rows, kHeadFloats * 4), "cudaMalloc rows");
+  if (st == G4_OK) st = check_cuda(ctx, cudaMalloc(&b.hbuf, kHFloats * 2), "cudaMalloc hbuf");
+  if (st == G4_OK) st = check_cuda(ctx, cudaMalloc(&b.ybuf, 3840 * 4), "cudaMalloc ybuf");
+  if (st == G4_OK) st = check_cuda(ctx, cudaMalloc(&b.attn, kAttnFloats * 4), "cudaMalloc attn");
+  if (st == G4_OK) st = check_cuda(ctx, cudaDeviceSynchronize(), "ctx init");
+  if (st != G4_OK) {
+    g4_ctx_destroy(ctx);
+    return st;
+  }
+  *out = ctx;
+  return G4_OK;
+}
+
+g4_status g4_ctx_destroy(g4_ctx* ctx) {
+  G4_CHECK_CTX(ctx);
+  cudaSetDevice(ctx->device);
+  if (ctx->comm && nccl().ok) nccl().comm_destroy(reinterpret_cast<ncclComm_t>(ctx->comm));
+  cudaFree(ctx->buf.scratch);
+  cudaFree(ctx->buf.part);
+  cudaFree(ctx->buf.rows);
+  cudaFree(ctx->buf.hbuf);
+  cudaFree(ctx->buf.ybuf);
+  cudaFree(ctx->buf.attn);
+  delete ctx;
+  return G4_OK;
+}
+
+g4_status g4_ctx_set_stream(g4_ctx* ctx, g4_stream_t stream) {
+  G4_CHECK_CTX(ctx);
+  ctx->stream = reinterpret_cast<cudaStream_t>(stream);
+  return G4_OK;
+}
+
+g4_status g4_nccl_unique_id(uint8_t out_id[128]) {
+  if (out_id == nullptr) return G4_ERR_BAD_ARG;
+  ncclUniqueId id;
+  if (!nccl().ok || nccl().get_unique_id(&id) != ncclSuccess) return G4_ERR_NCCL;
+  static_assert(sizeof(id) == 128, "ncclUniqueId is 128 bytes");
+  std::memcpy(out_id, &id, 128);
+  return G4_OK;
+}
+
+g4_status g4_ctx_init_tp(g4_ctx* ctx, int rank, int world, const uint8_t nccl_id[128]) {
+  G4_CHECK_CTX(ctx);
+  if (!(world == 1 || world == 2 || world == 4 || world == 8) || rank < 0 || rank >= world)
+    return fail(ctx, G4_ERR_BAD_ARG, "tensor-parallel world must be 1, 2, 4 or 8 and 0 <= rank < world");
+  ctx->tp_rank = rank;
+  ctx->tp_world = world;
+  if (world == 1) return G4_OK;
+  if (nccl_id == nullptr) return fail(ctx, G4_ERR_BAD_ARG, "nccl_id is null");
+  ncclUniqueId id;
+  std::memcpy(&id, nccl_id, 128);
+  cudaSetDevice(ctx->device);
+  ncclComm_t comm = nullptr;
+  if (!nccl().ok) return fail(ctx, G4_ERR_NCCL, "libnccl.so.2 could not be loaded");
+  const ncclResult_t r = nccl().comm_init_rank(&comm, world, id, rank);
+  if (r != ncclSuccess) return fail(ctx, G4_ERR_NCCL, std::string("ncclCommInitRank: ") + nccl().error_string(r));
+  ctx->comm = reinterpret_cast<ncclComm*>(comm);
+  return G4_OK;
+}
+
+const char* g4_ctx_last_error(const g4_ctx* ctx) { return ctx ? ctx->last_error.c_str() : "null context"; }
+
+g4_status g4_ctx_set_wait_budget(g4_ctx* ctx, uint32_t timeout_us) {
+  G4_CHECK_CTX(ctx);
+  if (timeout_us == 0) return fail(ctx, G4_ERR_BAD_ARG, "wait budget must be positive");
+  ctx->wait_budget_ns = static_cast<uint64_t>(timeout_us) * 1000ull;
+  return G4_OK;
+}
+
+g4_status g4_ctx_poll_device_status(g4_ctx* ctx, uint32_t* out_bits) {
+  G4_CHECK_CTX(ctx);
+  if (out_bits == nullptr) return fail(ctx, G4_ERR_BAD_ARG, "out_bits is null");
+  g4_status st = check_cuda(ctx, cudaStreamSynchronize(ctx->stream), "poll: stream sync");
+  if (st != G4_OK) return st;
+  uint32_t bits = 0;
+  st = check_cuda(ctx, cudaMemcpy(&bits, &ctx->buf.scratch->status, 4, cudaMemcpyDeviceToHost), "poll: read");
+  if (st != G4_OK) return st;
+  st = check_cuda(ctx, cudaMemset(&ctx->buf.scratch->status, 0, 4), "poll: clear");
+  if (st != G4_OK) return st;
+  *out_bits = bits;
+  if (bits & (DEV_ERR_TIMEOUT_MBAR | DEV_ERR_TIMEOUT_GRID | DEV_ERR_TIMEOUT_PEER))
+    return fail(ctx, G4_ERR_TIMEOUT, "a bounded device-side wait timed out (status " + std::to_string(bits) + ")");
+  if (bits & DEV_ERR_BAD_OFFSET) return fail(ctx, G4_ERR_BAD_ARG, "a device-resident offset was out of range");
+  return G4_OK;
+}
+
+g4_status g4_embed_token(g4_ctx* ctx, const g4_bf16* embedding_table, const int32_t* offset, g4_bf16* out) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, embedding_table, out);
+  G4_REQUIRE_SCALARS(ctx, offset);
+  return launch_embed(ctx, embedding_table, offset, out);
+}
+
+g4_status g4_copy_hidden_state(g4_ctx* ctx, const g4_bf16* x, g4_bf16* out) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, x, out);
+  return check_cuda(ctx, cudaMemcpyAsync(out, x, G4_H * 2, cudaMemcpyDeviceToDevice, ctx->stream),
+                    "copy_hidden_state");
+}
+
+g4_status g4_sliding_project_qkv(g4_ctx* ctx, const g4_bf16* x, const g4_f8e4m3* q_weight, const g4_f8e4m3* k_weight,
+                                 const g4_f8e4m3* v_weight, const g4_bf16* q_weight_scale,
+                                 const g4_bf16* k_weight_scale, const g4_bf16* v_weight_scale,
+                                 const g4_bf16* input_rms_weight, const g4_bf16* q_rms_weight,
+                                 const g4_bf16* k_rms_weight, const int32_t* kv_offset, const int32_t* rope_offset,
+                                 const g4_bf16* cos, const g4_bf16* sin, g4_bf16* k_cache, g4_bf16* v_cache,
+                                 g4_bf16* q_out) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, x, q_weight, k_weight, v_weight, input_rms_weight, q_rms_weight, k_rms_weight, cos, sin,
+                  k_cache, v_cache, q_out);
+  G4_REQUIRE_SCALARS(ctx, q_weight_scale, k_weight_scale, v_weight_scale, kv_offset, rope_offset);
+  const uint8_t* w[3] = {q_weight, k_weight, v_weight};
+  const uint8_t* bs[3] = {nullptr, nullptr, nullptr};
+  const uint16_t* rs[3] = {q_weight_scale, k_weight_scale, v_weight_scale};
+  const float* gs[3] = {nullptr, nullptr, nullptr};
+  return launch_qkv(ctx, false, false, x, w, bs, rs, gs, input_rms_weight, q_rms_weight, k_rms_weight, kv_offset,
+                    rope_offset, cos, sin, k_cache, v_cache, q_out);
+}
+
+g4_status g4_sliding_project_qkv_nvfp4(g4_ctx* ctx, const g4_bf16* x, const g4_f4x2* q_weight,
+                                       const g4_f4x2* k_weight, const g4_f4x2* v_weight,
+                                       const g4_f8e4m3* q_block_scale, const g4_f8e4m3* k_block_scale,
+                                       const g4_f8e4m3* v_block_scale, const float* q_global_scale,
+                                       const float* k_global_scale, const float* v_global_scale,
+                                       const g4_bf16* input_rms_weight, const g4_bf16* q_rms_weight,
+                                       const g4_bf16* k_rms_weight, const int32_t* kv_offset,
+                                       const int32_t* rope_offset, const g4_bf16* cos, const g4_bf16* sin,
+                                       g4_bf16* k_cache, g4_bf16* v_cache, g4_bf16* q_out) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, x, q_weight, k_weight, v_weight, q_block_scale, k_block_scale, v_block_scale,
+                  input_rms_weight, q_rms_weight, k_rms_weight, cos, sin, k_cache, v_cache, q_out);
+  G4_REQUIRE_SCALARS(ctx, q_global_scale, k_global_scale, v_global_scale, kv_offset, rope_offset);
+  const uint8_t* w[3] = {q_weight, k_weight, v_weight};
+  const uint8_t* bs[3] = {q_block_scale, k_block_scale, v_block_scale};
+  const uint16_t* rs[3] = {nullptr, nullptr, nullptr};
+  const float* gs[3] = {q_global_scale, k_global_scale, v_global_scale};
+  return launch_qkv(ctx, false, true, x, w, bs, rs, gs, input_rms_weight, q_rms_weight, k_rms_weight, kv_offset,
+                    rope_offset, cos, sin, k_cache, v_cache, q_out);
+}
+
+g4_status g4_full_project_qkv(g4_ctx* ctx, const g4_bf16* x, const g4_f8e4m3* q_weight, const g4_f8e4m3* k_weight,
+                              const g4_bf16* q_weight_scale, const g4_bf16* k_weight_scale,
+                              const g4_bf16* input_rms_weight, const g4_bf16* q_rms_weight,
+                              const g4_bf16* k_rms_weight, const int32_t* kv_offset, const int32_t* rope_offset,
+                              const g4_bf16* cos, const g4_bf16* sin, g4_bf16* k_cache, g4_bf16* v_cache,
+                              g4_bf16* q_out) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, x, q_weight, k_weight, input_rms_weight, q_rms_weight, k_rms_weight, cos, sin, k_cache,
+                  v_cache, q_out);
+  G4_REQUIRE_SCALARS(ctx, q_weight_scale, k_weight_scale, kv_offset, rope_offset);
+  const uint8_t* w[3] = {q_weight, k_weight, nullptr};
+  const uint8_t* bs[3] = {nullptr, nullptr, nullptr};
+  const uint16_t* rs[3] = {q_weight_scale, k_weight_scale, nullptr};
+  const float* gs[3] = {nullptr, nullptr, nullptr};
+  return launch_qkv(ctx, true, false, x, w, bs, rs, gs, input_rms_weight, q_rms_weight, k_rms_weight, kv_offset,
+                    rope_offset, cos, sin, k_cache, v_cache, q_out);
+}
+
+g4_status g4_sliding_attention(g4_ctx* ctx, const g4_bf16* q, const g4_bf16* k, const g4_bf16* v, const float* mask,
+                               g4_bf16* out) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, q, k, v, mask, out);
+  return launch_sliding_attention(ctx, q, k, v, mask, out);
+}
+
+g4_status g4_sliding_attention_output(g4_ctx* ctx, const g4_bf16* x, const g4_bf16* post_attn_rms_weight,
+                                      const g4_f8e4m3* o_weight, const g4_bf16* o_weight_scale,
+                                      g4_bf16* residual) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, x, post_attn_rms_weight, o_weight, residual);
+  G4_REQUIRE_SCALARS(ctx, o_weight_scale);
+  return launch_oproj(ctx, false, false, x, nullptr, post_attn_rms_weight, o_weight, nullptr, o_weight_scale, nullptr,
+                      residual);
+}
+
+g4_status g4_sliding_attention_output_nvfp4(g4_ctx* ctx, const g4_bf16* x, const g4_bf16* post_attn_rms_weight,
+                                            const g4_f4x2* o_weight, const g4_f8e4m3* o_block_scale,
+                                            const float* o_global_scale, g4_bf16* residual) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, x, post_attn_rms_weight, o_weight, o_block_scale, residual);
+  G4_REQUIRE_SCALARS(ctx, o_global_scale);
+  return launch_oproj(ctx, false, true, x, nullptr, post_attn_rms_weight, o_weight, o_block_scale, nullptr,
+                      o_global_scale, residual);
+}
+
+g4_status g4_full_attention_first_page(g4_ctx* ctx, const g4_bf16* q, const g4_bf16* k, const g4_bf16* v,
+                                       const float* mask, float* running_max, float* running_sum, g4_bf16* out) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, q, k, v, mask, out);
+  G4_REQUIRE_SCALARS(ctx, running_max, running_sum);
+  return launch_full_page(ctx, true, q, k, v, mask, running_max, running_sum, out);
+}
+
+g4_status g4_full_attention_page(g4_ctx* ctx, const g4_bf16* q, const g4_bf16* k, const g4_bf16* v, const float* mask,
+                                 float* running_max, float* running_sum, g4_bf16* out) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, q, k, v, mask, out);
+  G4_REQUIRE_SCALARS(ctx, running_max, running_sum);
+  return launch_full_page(ctx, false, q, k, v, mask, running_max, running_sum, out);
+}
+
+g4_status g4_full_attention_paged(g4_ctx* ctx, const g4_bf16* q, const g4_bf16* const* k_pages,
+                                  const g4_bf16* const* v_pages, int n_pages, int last_row, float* running_sum,
+                                  g4_bf16* out) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, q, out);
+  G4_REQUIRE_SCALARS(ctx, k_pages, v_pages, running_sum);
+  if (n_pages < 1 || n_pages > G4_E / G4_TF || last_row < 0 || last_row >= G4_TF)
+    return fail(ctx, G4_ERR_BAD_ARG, "n_pages must be in [1, 64] and last_row in [0, 511]");
+  return launch_full_paged(ctx, q, k_pages, v_pages, n_pages, last_row, running_sum, out);
+}
+
+g4_status g4_full_attention_output(g4_ctx* ctx, const g4_bf16* x, const float* running_sum,
+                                   const g4_bf16* post_attn_rms_weight, const g4_f8e4m3* o_weight,
+                                   const g4_bf16* o_weight_scale, g4_bf16* residual) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, x, post_attn_rms_weight, o_weight, residual);
+  G4_REQUIRE_SCALARS(ctx, running_sum, o_weight_scale);
+  return launch_oproj(ctx, true, false, x, running_sum, post_attn_rms_weight, o_weight, nullptr, o_weight_scale,
+                      nullptr, residual);
+}
+
+g4_status g4_decoder_feedforward(g4_ctx* ctx, g4_bf16* residual, const g4_bf16* pre_ff_rms_weight,
+                                 const g4_f4x2* up_weight_packed, const g4_f4x2* gate_weight_packed,
+                                 const g4_f4x2* down_weight_packed, const g4_f8e4m3* up_weight_scale,
+                                 const g4_f8e4m3* gate_weight_scale, const g4_f8e4m3* down_weight_scale,
+                                 const float* up_global_scale, const float* gate_global_scale,
+                                 const float* down_global_scale, const g4_bf16* post_ff_rms_weight,
+                                 const g4_bf16* layer_scalar) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, residual, pre_ff_rms_weight, up_weight_packed, gate_weight_packed, down_weight_packed,
+                  up_weight_scale, gate_weight_scale, down_weight_scale, post_ff_rms_weight, layer_scalar);
+  G4_REQUIRE_SCALARS(ctx, up_global_scale, gate_global_scale, down_global_scale);
+  return launch_decoder_feedforward(ctx, residual, pre_ff_rms_weight, up_weight_packed, gate_weight_packed,
+                                    down_weight_packed, up_weight_scale, gate_weight_scale, down_weight_scale,
+                                    up_global_scale, gate_global_scale, down_global_scale, post_ff_rms_weight,
+                                    layer_scalar);
+}
+
+g4_status g4_final_norm_and_logits(g4_ctx* ctx, const g4_bf16* input, const g4_bf16* rms_weight,
+                                   const g4_bf16* lm_head_weight, g4_bf16* out) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, input, rms_weight, lm_head_weight, out);
+  return launch_lm_head(ctx, input, rms_weight, lm_head_weight, out);
+}
+
+g4_status g4_argmax_bf16(g4_ctx* ctx, const g4_bf16* logits, int n, int32_t* out_index) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, logits);
+  G4_REQUIRE_SCALARS(ctx, out_index);
+  if (n <= 0) return fail(ctx, G4_ERR_BAD_ARG, "n must be positive");
+  return launch_argmax(ctx, logits, n, out_index);
+}
+
+g4_status g4_dequant_nvfp4(g4_ctx* ctx, const g4_f4x2* packed, const g4_f8e4m3* block_scale, int rows, int cols,
+                           g4_bf16* out) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, packed, block_scale, out);
+  if (rows <= 0 || cols <= 0 || cols % 16 != 0) return fail(ctx, G4_ERR_BAD_ARG, "cols must be a positive multiple of 16");
+  return launch_dequant_nvfp4(ctx, packed, block_scale, rows, cols, out);
+}
+
+g4_status g4_dequant_fp8(g4_ctx* ctx, const g4_f8e4m3* weight, int64_t count, g4_bf16* out) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, weight, out);
+  if (count <= 0) return fail(ctx, G4_ERR_BAD_ARG, "count must be positive");
+  return launch_dequant_fp8(ctx, weight, count, out);
+}
+
+}  // extern "C"

@@ -1,0 +1,75 @@
+// Host-side context and device scratch layout shared by the g4b200 translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/g4.h"
+
+struct ncclComm;
+
+namespace g4 {
+
+// Device scratch owned by a context.  Counters are zero at creation and every kernel
+// that uses one returns it to zero before it exits, so launches (and CUDA-graph
+// replays) need no host-side reset.
+struct Scratch {
+  uint32_t status;            // DEV_ERR_* bits raised by kernels (sticky until polled)
+  uint32_t mlp_sync;          // MLP: CTAs that finished the gate/up phase
+  uint32_t mlp_done;          // MLP: CTAs that finished the down phase
+  uint32_t mlp_amax;          // MLP: bits of max |h| over the intermediate vector
+  uint32_t proj_done;         // o-proj: CTAs done
+  uint32_t lm_done;           // (reserved)
+  uint32_t pad0[2];
+  uint32_t head_count[64];    // qkv: completed items per head group
+  uint32_t attn_count[64];    // split-KV attention: completed chunks per kv head
+  uint32_t attn_done;         // paged attention: CTAs done
+  uint32_t pad1[31];
+};
+
+constexpr size_t kPartFloats = 16 * 3840 * 2;     // row-parallel partial sums
+constexpr size_t kHeadFloats = 8192 + 512 + 8192; // raw projection rows (qkv)
+constexpr size_t kHFloats = 15360;                // MLP intermediate (bf16 stored)
+constexpr size_t kAttnFloats = 512 * (2 * 16 + 16 * 512) + 4096;  // 512 chunks of 16 heads
+
+struct DeviceBuffers {
+  Scratch* scratch = nullptr;
+  float* part = nullptr;     // [kPartFloats]
+  float* rows = nullptr;     // [kHeadFloats]
+  uint16_t* hbuf = nullptr;  // [kHFloats] bf16
+  float* ybuf = nullptr;     // [3840] f32 (TP all-reduce buffer)
+  float* attn = nullptr;     // [kAttnFloats] split-KV partials
+};
+
+}  // namespace g4
+
+struct g4_ctx {
+  int device = 0;
+  int sm_count = 0;
+  cudaStream_t stream = nullptr;
+  int tp_rank = 0;
+  int tp_world = 1;
+  ncclComm* comm = nullptr;
+  uint64_t wait_budget_ns = 2000000000ull;  // 2 s
+  g4::DeviceBuffers buf;
+  std::string last_error;
+  bool coop_ok = true;
+};
+
+namespace g4 {
+
+g4_status fail(g4_ctx* ctx, g4_status code, const std::string& msg);
+g4_status check_cuda(g4_ctx* ctx, cudaError_t err, const char* what);
+bool aligned16(const void* p);
+
+// Launchers implemented in the kernel translation units.
+g4_status launch_decoder_feedforward(g4_ctx* ctx, uint16_t* residual, const uint16_t* pre_w,
+                                     const uint8_t* up_p, const uint8_t* gate_p, const uint8_t* down_p,
+                                     const uint8_t* up_s, const uint8_t* gate_s, const uint8_t* down_s,
+                                     const float* up_gs, const float* gate_gs, const float* down_gs,
+                                     const uint16_t* post_w, const uint16_t* layer_scalar);
+g4_status allreduce_f32(g4_ctx* ctx, float* buf, size_t count);
+
+}  // namespace g4

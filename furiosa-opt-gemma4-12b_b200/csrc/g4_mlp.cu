@@ -1,0 +1,246 @@
+// decoder_feedforward: the NVFP4 GeGLU MLP block of one decode token, ONE persistent
+// cooperative launch (drop-in for ops::decoder_feedforward, src/ops.rs:213-253).
+//
+//   phase 0  stage:   x = RMSNorm(residual, pre_ff)           (src/device/shared/rmsnorm.rs)
+//   phase 0  items:   8 gate rows + the same 8 up rows per item;
+//                     epilogue h = bf16(gelu_tanh(bf16(bf16(g)*gs_g)) * bf16(bf16(u)*gs_u))
+//                     (mlp.rs:13-155 projection, :218-334 GeGLU; tanh per the oracle)
+//   grid wait:        every CTA's h rows are visible (bounded spin, error flag on timeout)
+//   phase 1  stage:   h as scaled f16 (max |h| gathered with atomicMax in phase 0)
+//   phase 1  items:   8 down rows x 3840-wide K quarter each (mlp.rs:339-437), partial
+//                     sums to scratch
+//   final (last CTA): y = bf16(bf16(sum)*gs_d); residual = bf16(bf16(residual +
+//                     RMSNorm(y, post_ff)) * layer_scalar)   (ops.rs:248-252, residual.rs)
+//
+// The producer warp never waits for the grid: it streams phase-1 down weights while the
+// last gate/up items of other CTAs finish, so the phase boundary costs no HBM time.
+// Under tensor parallelism the last CTA instead writes the f32 partial y, which the
+// host all-reduces before the norm epilogue kernel.
+#include "g4_internal.h"
+#include "g4_stream.cuh"
+
+namespace g4 {
+
+struct MlpOp {
+  static constexpr Fmt kFmt = Fmt::NVFP4;
+  static constexpr int kPhases = 2;
+
+  uint16_t* residual;
+  const uint16_t* pre_w;
+  const uint16_t* post_w;
+  const uint16_t* layer_scalar;
+  const uint8_t* up_p;
+  const uint8_t* gate_p;
+  const uint8_t* down_p;
+  const uint8_t* up_s;
+  const uint8_t* gate_s;
+  const uint8_t* down_s;
+  const float* up_gs;
+  const float* gate_gs;
+  const float* down_gs;
+  Scratch* scr;
+  float* part;
+  uint16_t* hbuf;
+  float* ybuf;      // TP: f32 partial y for the all-reduce (nullptr: fused epilogue)
+  int lrows;        // local intermediate rows (L / tp)
+  int kc;           // down K per unit (3840, or lrows when smaller)
+  int kq;           // down units per row tile = lrows / kc
+  UnitGeom g0, g1;
+
+  __device__ int items(int ph) const { return ph == 0 ? lrows / 8 : (H / 8) * kq; }
+  __device__ UnitGeom geom(int ph) const { return ph == 0 ? g0 : g1; }
+  __device__ UnitDesc unit(int ph, int it, int half) const {
+    UnitDesc u;
+    if (ph == 0) {
+      const uint8_t* p = half ? up_p : gate_p;
+      const uint8_t* s = half ? up_s : gate_s;
+      u.codes = p + static_cast<size_t>(it) * 8 * (H / 2);
+      u.scales = s + static_cast<size_t>(it) * 8 * (H / 16);
+      u.code_stride = H / 2;
+      u.scale_stride = H / 16;
+      u.xoff = 0;
+    } else {
+      if (half) {
+        u.codes = nullptr;
+        return u;
+      }
+      const int r = it / kq, q = it % kq;
+      const size_t cstride = lrows / 2, sstride = lrows / 16;
+      u.codes = down_p + static_cast<size_t>(r) * 8 * cstride + static_cast<size_t>(q) * (kc / 2);
+      u.scales = down_s + static_cast<size_t>(r) * 8 * sstride + static_cast<size_t>(q) * (kc / 16);
+      u.code_stride = static_cast<uint32_t>(cstride);
+      u.scale_stride = static_cast<uint32_t>(sstride);
+      u.xoff = q * kc;
+    }
+    return u;
+  }
+  __device__ uint32_t* status() const { return &scr->status; }
+  __device__ uint32_t* done_counter() const { return &scr->mlp_done; }
+  __device__ bool has_final() const { return true; }
+
+  __device__ void stage(StreamSmem& sm, uint8_t* xbuf, int ph, int tid) const {
+    uint16_t* xs = reinterpret_cast<uint16_t*>(xbuf);
+    if (ph == 0) {
+      const int e = stage_rmsnorm(residual, pre_w, H, xs, true, sm.scratch);
+      if (tid == 0) {
+        sm.xexp = e;
+        sm.scratch[40] = __ldg(gate_gs);
+        sm.scratch[41] = __ldg(up_gs);
+      }
+    } else {
+      const float amax = __uint_as_float(ld_acquire_gpu(&scr->mlp_amax));
+      const int e = f16_scale_exponent(amax);
+      const float sc = ldexpf(1.0f, e);
+      for (int i = tid; i < lrows; i += kConsumerThreads) xs[i] = f32_to_f16(bf16_to_f32(__ldcg(hbuf + i)) * sc);
+      if (tid == 0) sm.xexp = e;
+    }
+  }
+
+  __device__ bool between_phases(StreamSmem& sm, int ph, uint64_t deadline) const {
+    return grid_wait(&scr->mlp_sync, gridDim.x, deadline, &scr->status, sm);
+  }
+
+  __device__ void item_epilogue(StreamSmem& sm, int ph, int it, int lane, float v) const {
+    const float unscale = ldexpf(1.0f, -sm.xexp);
+    if (ph == 0) {
+      const float up = __shfl_down_sync(0xffffffffu, v, 8);
+      float hv = 0.f;
+      if (lane < 8) {
+        const float g2 = round_bf16(round_bf16(v * unscale) * sm.scratch[40]);
+        const float u2 = round_bf16(round_bf16(up * unscale) * sm.scratch[41]);
+        hv = round_bf16(round_bf16(gelu_tanh(g2)) * u2);
+        hbuf[it * 8 + lane] = f32_to_bf16(hv);
+      }
+      const float m = warp_max(fabsf(hv));
+      if (lane == 0) atomicMax(&scr->mlp_amax, __float_as_uint(m));
+    } else {
+      if (lane < 8) {
+        const int r = it / kq, q = it % kq;
+        part[q * H + r * 8 + lane] = v * unscale;
+      }
+    }
+  }
+
+  __device__ void final_epilogue(StreamSmem& sm, uint8_t* xbuf, int tid) const {
+    float* y = reinterpret_cast<float*>(xbuf);
+    for (int n = tid; n < H; n += kConsumerThreads) {
+      float s = 0.f;
+      for (int q = 0; q < kq; ++q) s += __ldcg(part + q * H + n);
+      y[n] = s;
+    }
+    if (ybuf != nullptr) {
+      for (int n = tid; n < H; n += kConsumerThreads) ybuf[n] = y[n];
+    } else {
+      const float gsd = __ldg(down_gs);
+      float ss = 0.f;
+      for (int n = tid; n < H; n += kConsumerThreads) {
+        const float d2 = round_bf16(round_bf16(y[n]) * gsd);
+        y[n] = d2;
+        ss = __fadd_rn(ss, __fmul_rn(d2, d2));
+      }
+      const float r = rms_factor(consumer_sum(ss, sm.scratch), H);
+      const float ls = bf16_to_f32(layer_scalar[0]);
+      for (int n = tid; n < H; n += kConsumerThreads) {
+        const float nb = round_bf16(__fmul_rn(__fmul_rn(y[n], r), bf16_to_f32(post_w[n])));
+        const float r2 = round_bf16(__fadd_rn(bf16_to_f32(residual[n]), nb));
+        residual[n] = f32_to_bf16(__fmul_rn(r2, ls));
+      }
+    }
+    if (tid == 0) {
+      scr->mlp_sync = 0u;
+      scr->mlp_amax = 0u;
+    }
+  }
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    mlp_kernel(const MlpOp op, const StreamLayout lay, uint32_t slot_bytes, uint64_t budget_ns) {
+  stream_body(op, lay, slot_bytes, budget_ns);
+}
+
+// TP epilogue after the all-reduce of y (one CTA): the same math as the fused tail.
+__global__ void __launch_bounds__(1024) mlp_tp_epilogue_kernel(const float* __restrict__ y, const float* down_gs,
+                                                               const uint16_t* __restrict__ post_w,
+                                                               const uint16_t* __restrict__ layer_scalar,
+                                                               uint16_t* __restrict__ residual) {
+  __shared__ float red[32];
+  __shared__ float yb[H];
+  const float gsd = __ldg(down_gs);
+  float ss = 0.f;
+  for (int n = threadIdx.x; n < H; n += blockDim.x) {
+    const float d2 = round_bf16(round_bf16(y[n]) * gsd);
+    yb[n] = d2;
+    ss = __fadd_rn(ss, __fmul_rn(d2, d2));
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) tot += red[w];
+  const float r = rms_factor(tot, H);
+  const float ls = bf16_to_f32(layer_scalar[0]);
+  for (int n = threadIdx.x; n < H; n += blockDim.x) {
+    const float nb = round_bf16(__fmul_rn(__fmul_rn(yb[n], r), bf16_to_f32(post_w[n])));
+    const float r2 = round_bf16(__fadd_rn(bf16_to_f32(residual[n]), nb));
+    residual[n] = f32_to_bf16(__fmul_rn(r2, ls));
+  }
+}
+
+static constexpr uint32_t kMlpSlots = 8;
+
+g4_status launch_decoder_feedforward(g4_ctx* ctx, uint16_t* residual, const uint16_t* pre_w, const uint8_t* up_p,
+                                     const uint8_t* gate_p, const uint8_t* down_p, const uint8_t* up_s,
+                                     const uint8_t* gate_s, const uint8_t* down_s, const float* up_gs,
+                                     const float* gate_gs, const float* down_gs, const uint16_t* post_w,
+                                     const uint16_t* layer_scalar) {
+  MlpOp op;
+  op.residual = residual;
+  op.pre_w = pre_w;
+  op.post_w = post_w;
+  op.layer_scalar = layer_scalar;
+  op.up_p = up_p;
+  op.gate_p = gate_p;
+  op.down_p = down_p;
+  op.up_s = up_s;
+  op.gate_s = gate_s;
+  op.down_s = down_s;
+  op.up_gs = up_gs;
+  op.gate_gs = gate_gs;
+  op.down_gs = down_gs;
+  op.scr = ctx->buf.scratch;
+  op.part = ctx->buf.part;
+  op.hbuf = ctx->buf.hbuf;
+  op.ybuf = ctx->tp_world > 1 ? ctx->buf.ybuf : nullptr;
+  op.lrows = L / ctx->tp_world;
+  op.kc = (op.lrows % 3840 == 0) ? 3840 : op.lrows;
+  op.kq = op.lrows / op.kc;
+  op.g0 = make_geom(H / 2, H / 16, true);
+  op.g1 = make_geom(op.kc / 2, op.kc / 16, op.kq == 1);
+  if (op.g1.sb % 16 != 0 && !op.g1.scale_block) return fail(ctx, G4_ERR_UNSUPPORTED, "MLP shard scale layout");
+  const uint32_t slot_bytes = op.g0.slot_bytes > op.g1.slot_bytes ? op.g0.slot_bytes : op.g1.slot_bytes;
+  const StreamLayout lay = make_layout(slot_bytes, kMlpSlots, static_cast<uint32_t>(op.lrows > H ? op.lrows : H) * 4);
+  static bool attr_set[16] = {};
+  if (!attr_set[ctx->device & 15]) {
+    g4_status st = check_cuda(ctx, cudaFuncSetAttribute(mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                        static_cast<int>(lay.total)),
+                              "cudaFuncSetAttribute(mlp)");
+    if (st != G4_OK) return st;
+    attr_set[ctx->device & 15] = true;
+  }
+  const uint64_t budget = ctx->wait_budget_ns;
+  void* args[] = {(void*)&op, (void*)&lay, (void*)&slot_bytes, (void*)&budget};
+  dim3 grid(ctx->sm_count), block(kThreads);
+  g4_status st = check_cuda(
+      ctx, cudaLaunchCooperativeKernel((const void*)mlp_kernel, grid, block, args, lay.total, ctx->stream),
+      "launch mlp_kernel");
+  if (st != G4_OK) return st;
+  if (ctx->tp_world > 1) {
+    st = allreduce_f32(ctx, ctx->buf.ybuf, H);
+    if (st != G4_OK) return st;
+    mlp_tp_epilogue_kernel<<<1, 1024, 0, ctx->stream>>>(ctx->buf.ybuf, down_gs, post_w, layer_scalar, residual);
+    st = check_cuda(ctx, cudaGetLastError(), "launch mlp_tp_epilogue");
+  }
+  return st;
+}
+
+}  // namespace g4

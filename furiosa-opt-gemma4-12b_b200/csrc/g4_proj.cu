@@ -1,0 +1,499 @@
+// Attention projections and the lm_head on the streaming engine.
+//
+//  QkvOp   : {sliding,full}_project_qkv (src/ops.rs:44-124).  Stage RMSNorm(x); items
+//            cover 8 rows of the concatenated [Q;K;V] row space (FP8: both K halves in
+//            one item; NVFP4: two row tiles); each item stores raw row sums and bumps its
+//            head's counter; the warp completing a head runs the head epilogue: row scale
+//            -> bf16, per-head RMSNorm (q/k weighted, v unweighted; full layers derive V
+//            from the raw K head, src/device/full/rmsnorm.rs:189-196), RoPE with the
+//            kernel-convention tables (sin low half pre-negated, src/host/runtime.rs:
+//            271-299), then q_out or the KV-cache row at the device byte offset.
+//  OprojOp : {sliding,full}_attention_output (src/ops.rs:138-211).  Stage x (full: x/sum
+//            per head first, src/device/full/attention.rs:336-358); items = 8 output rows
+//            x two K chunks; last CTA: y -> bf16(y*row_scale) -> RMSNorm(post) -> +residual.
+//  LmHeadOp: final_norm_and_logits (src/ops.rs:255-312, src/device/shared/lm_head.rs):
+//            stage RMSNorm(x) as bf16; items = 8 vocab rows x both K halves; epilogue
+//            bf16 logit -> bf16(tanh(l/30)*30).
+#include "g4_internal.h"
+#include "g4_stream.cuh"
+
+namespace g4 {
+
+// ============================================================================ QKV
+struct QkvOp {
+  static constexpr int kPhases = 1;
+  // geometry
+  int D;            // head dim (256 sliding, 512 full)
+  int nq, nk, nv;   // local q / k / v heads (nv = 0: V derived from raw K)
+  int nvfp4;        // 1: NVFP4 weights (two row tiles per item), 0: FP8 (two K halves)
+  // inputs
+  const uint16_t* x;
+  const uint16_t* in_w;
+  const uint8_t* w[3];       // codes of Q, K, V
+  const uint8_t* bs[3];      // NVFP4 block scales
+  const uint16_t* rs[3];     // FP8 per-row bf16 scales
+  const float* gs[3];        // NVFP4 reciprocal global scales
+  const uint16_t* qn_w;
+  const uint16_t* kn_w;
+  const int32_t* kv_off;
+  const int32_t* rope_off;
+  const uint16_t* cosT;
+  const uint16_t* sinT;
+  long long table_elems;     // E * D
+  uint16_t* kc;
+  uint16_t* vc;
+  long long cache_elems;
+  uint16_t* q_out;
+  Scratch* scr;
+  float* rows;               // raw row sums of the concatenated row space
+  UnitGeom g;
+
+  __device__ int total_rows() const { return (nq + nk + nv) * D; }
+  __device__ int items() const { return nvfp4 ? total_rows() / 16 : total_rows() / 8; }
+  __device__ int items(int) const { return items(); }
+  __device__ UnitGeom geom(int) const { return g; }
+  // matrix index and local row of a concatenated row
+  __device__ void locate(int row, int& m, int& r) const {
+    if (row < nq * D) {
+      m = 0;
+      r = row;
+    } else if (row < (nq + nk) * D) {
+      m = 1;
+      r = row - nq * D;
+    } else {
+      m = 2;
+      r = row - (nq + nk) * D;
+    }
+  }
+  __device__ UnitDesc unit(int, int it, int half) const {
+    UnitDesc u;
+    int row0, koff;
+    if (nvfp4) {
+      row0 = it * 16 + half * 8;
+      koff = 0;
+    } else {
+      row0 = it * 8;
+      koff = half * (H / 2);
+    }
+    int m, r;
+    locate(row0, m, r);
+    const uint32_t rowbytes = nvfp4 ? H / 2 : H;
+    u.codes = w[m] + static_cast<size_t>(r) * rowbytes + (nvfp4 ? 0 : koff);
+    u.scales = nvfp4 ? bs[m] + static_cast<size_t>(r) * (H / 16) : nullptr;
+    u.code_stride = rowbytes;
+    u.scale_stride = H / 16;
+    u.xoff = koff;
+    return u;
+  }
+  __device__ uint32_t* status() const { return &scr->status; }
+  __device__ uint32_t* done_counter() const { return &scr->proj_done; }
+  __device__ bool has_final() const { return false; }
+  __device__ bool between_phases(StreamSmem&, int, uint64_t) const { return true; }
+  __device__ void final_epilogue(StreamSmem&, uint8_t*, int) const {}
+  __device__ void stage(StreamSmem& sm, uint8_t* xbuf, int, int tid) const {
+    const int e = stage_rmsnorm(x, in_w, H, reinterpret_cast<uint16_t*>(xbuf), true, sm.scratch);
+    if (tid == 0) sm.xexp = e;
+  }
+
+  // Projection value of one row before the per-head norm: FP8 bf16(acc*scale_row),
+  // NVFP4 bf16(bf16(acc)*global).
+  __device__ float row_value(int row, float acc) const {
+    int m, r;
+    locate(row, m, r);
+    if (nvfp4) return round_bf16(round_bf16(acc) * __ldg(gs[m]));
+    return round_bf16(acc * bf16_to_f32(rs[m][r]));
+  }
+
+  __device__ void item_epilogue(StreamSmem& sm, int, int it, int lane, float v) const {
+    const float unscale = ldexpf(1.0f, -sm.xexp);
+    int row0, nrows;
+    if (nvfp4) {
+      row0 = it * 16;
+      nrows = 16;
+      if (lane < 16) rows[row0 + lane] = v * unscale;
+    } else {
+      row0 = it * 8;
+      nrows = 8;
+      const float other = __shfl_down_sync(0xffffffffu, v, 8);
+      if (lane < 8) rows[row0 + lane] = (v + other) * unscale;
+    }
+    __syncwarp();
+    const int head = row0 / D;
+    uint32_t old = 0;
+    if (lane == 0) {
+      __threadfence();
+      old = atom_add_acq_rel_gpu(&scr->head_count[head], 1u);
+    }
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old + 1 == static_cast<uint32_t>(D / nrows)) {
+      __threadfence();
+      head_epilogue(head, lane);
+      if (lane == 0) scr->head_count[head] = 0u;
+    }
+  }
+
+  // Warp-level: norm + RoPE + store of one head.  Lane l owns elements l + 32j.
+  __device__ void head_epilogue(int head, int lane) const {
+    constexpr int kMaxJ = 16;
+    const int J = D / 32;
+    float raw[kMaxJ];
+    const int row0 = head * D;
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxJ; ++j) {
+      if (j < J) {
+        raw[j] = row_value(row0 + lane + 32 * j, __ldcg(rows + row0 + lane + 32 * j));
+        ss = __fadd_rn(ss, __fmul_rn(raw[j], raw[j]));
+      }
+    }
+    const float r = rms_factor(warp_sum(ss), D);
+    const bool is_q = head < nq;
+    const bool is_k = !is_q && head < nq + nk;
+    const int roff = __ldg(rope_off) / 2;
+    const int koff = __ldg(kv_off) / 2;
+    if (roff < 0 || static_cast<long long>(roff) + D > table_elems || koff < 0 ||
+        static_cast<long long>(koff) + static_cast<long long>(nk > 0 ? (nv > 0 ? nk : 1) : 1) * D > cache_elems) {
+      if (lane == 0) atomicOr(&scr->status, DEV_ERR_BAD_OFFSET);
+      return;
+    }
+    // V of a full (MQA) layer: unweighted norm of the raw K head.
+    if (is_k && nv == 0) {
+      for (int j = 0; j < J; ++j) {
+        const int i = lane + 32 * j;
+        vc[koff + i] = f32_to_bf16(__fmul_rn(raw[j], r));
+      }
+    }
+    if (!is_q && !is_k) {  // sliding V head: unweighted norm, no RoPE
+      const int vh = head - nq - nk;
+      for (int j = 0; j < J; ++j) {
+        const int i = lane + 32 * j;
+        vc[koff + vh * D + i] = f32_to_bf16(__fmul_rn(raw[j], r));
+      }
+      return;
+    }
+    const uint16_t* nw = is_q ? qn_w : kn_w;
+    float n[kMaxJ];
+#pragma unroll
+    for (int j = 0; j < kMaxJ; ++j)
+      if (j < J) n[j] = round_bf16(__fmul_rn(__fmul_rn(raw[j], r), bf16_to_f32(nw[lane + 32 * j])));
+    const int half = J / 2;
+#pragma unroll
+    for (int j = 0; j < kMaxJ; ++j) {
+      if (j < J) {
+        const int i = lane + 32 * j;
+        const int pj = (j < half) ? j + half : j - half;
+        float partner = 0.f;
+#pragma unroll
+        for (int q = 0; q < kMaxJ; ++q)
+          if (q == pj) partner = n[q];
+        const float c = bf16_to_f32(cosT[roff + i]);
+        const float s = bf16_to_f32(sinT[roff + i]);
+        const float o = round_bf16(__fadd_rn(round_bf16(__fmul_rn(n[j], c)), round_bf16(__fmul_rn(partner, s))));
+        if (is_q) {
+          q_out[head * D + i] = f32_to_bf16(o);
+        } else {
+          const int kh = head - nq;
+          kc[koff + kh * D + i] = f32_to_bf16(o);
+        }
+      }
+    }
+  }
+};
+
+// ============================================================================ o-proj
+struct OprojOp {
+  static constexpr int kPhases = 1;
+  int K;            // local input width
+  int kc;           // K per unit
+  int kq;           // units per row tile
+  int nvfp4;
+  int Dh;           // head dim for the running-sum division (0: none)
+  const uint16_t* x;
+  const float* rsum;
+  const uint16_t* post_w;
+  const uint8_t* w;
+  const uint8_t* bs;
+  const uint16_t* row_scale;
+  const float* gsc;
+  uint16_t* residual;
+  Scratch* scr;
+  float* part;
+  float* ybuf;      // TP: partial y (already unscaled) for the all-reduce
+  UnitGeom g;
+
+  __device__ int pairs() const { return (kq + 1) / 2; }
+  __device__ int items(int) const { return (H / 8) * pairs(); }
+  __device__ UnitGeom geom(int) const { return g; }
+  __device__ UnitDesc unit(int, int it, int half) const {
+    UnitDesc u;
+    const int r = it / pairs(), p = it % pairs();
+    const int q = 2 * p + half;
+    if (q >= kq) {
+      u.codes = nullptr;
+      return u;
+    }
+    const uint32_t rowbytes = nvfp4 ? K / 2 : K;
+    const uint32_t unitbytes = nvfp4 ? kc / 2 : kc;
+    u.codes = w + static_cast<size_t>(r) * 8 * rowbytes + static_cast<size_t>(q) * unitbytes;
+    u.scales = nvfp4 ? bs + static_cast<size_t>(r) * 8 * (K / 16) + static_cast<size_t>(q) * (kc / 16) : nullptr;
+    u.code_stride = rowbytes;
+    u.scale_stride = K / 16;
+    u.xoff = q * kc;
+    return u;
+  }
+  __device__ uint32_t* status() const { return &scr->status; }
+  __device__ uint32_t* done_counter() const { return &scr->proj_done; }
+  __device__ bool has_final() const { return true; }
+  __device__ bool between_phases(StreamSmem&, int, uint64_t) const { return true; }
+
+  __device__ void stage(StreamSmem& sm, uint8_t* xbuf, int, int tid) const {
+    uint16_t* xs = reinterpret_cast<uint16_t*>(xbuf);
+    float amax = 0.f;
+    for (int i = tid; i < K; i += kConsumerThreads) {
+      float v = bf16_to_f32(x[i]);
+      if (Dh > 0) v = round_bf16(__fdiv_rn(v, __ldg(rsum + i / Dh)));
+      xs[i] = f32_to_bf16(v);
+      amax = fmaxf(amax, fabsf(v));
+    }
+    const int e = f16_scale_exponent(consumer_max(amax, sm.scratch + 32));
+    const float sc = ldexpf(1.0f, e);
+    for (int i = tid; i < K; i += kConsumerThreads) xs[i] = f32_to_f16(bf16_to_f32(xs[i]) * sc);
+    if (tid == 0) sm.xexp = e;
+  }
+
+  __device__ void item_epilogue(StreamSmem& sm, int, int it, int lane, float v) const {
+    const float other = __shfl_down_sync(0xffffffffu, v, 8);
+    if (lane < 8) {
+      const int r = it / pairs(), p = it % pairs();
+      part[p * H + r * 8 + lane] = (v + other) * ldexpf(1.0f, -sm.xexp);
+    }
+  }
+
+  __device__ float proj_value(int n, float y) const {
+    if (nvfp4) return round_bf16(round_bf16(y) * __ldg(gsc));
+    return round_bf16(y * bf16_to_f32(row_scale[n]));
+  }
+
+  __device__ void final_epilogue(StreamSmem& sm, uint8_t* xbuf, int tid) const {
+    float* y = reinterpret_cast<float*>(xbuf);
+    const int P = pairs();
+    for (int n = tid; n < H; n += kConsumerThreads) {
+      float s = 0.f;
+      for (int p = 0; p < P; ++p) s += __ldcg(part + p * H + n);
+      y[n] = s;
+    }
+    if (ybuf != nullptr) {
+      for (int n = tid; n < H; n += kConsumerThreads) ybuf[n] = y[n];
+      return;
+    }
+    float ss = 0.f;
+    for (int n = tid; n < H; n += kConsumerThreads) {
+      const float pv = proj_value(n, y[n]);
+      y[n] = pv;
+      ss = __fadd_rn(ss, __fmul_rn(pv, pv));
+    }
+    const float r = rms_factor(consumer_sum(ss, sm.scratch), H);
+    for (int n = tid; n < H; n += kConsumerThreads) {
+      const float nb = round_bf16(__fmul_rn(__fmul_rn(y[n], r), bf16_to_f32(post_w[n])));
+      residual[n] = f32_to_bf16(__fadd_rn(bf16_to_f32(residual[n]), nb));
+    }
+  }
+};
+
+// TP tail of the o-proj after the all-reduce of y.
+__global__ void __launch_bounds__(1024) oproj_tp_epilogue_kernel(const float* __restrict__ y, int nvfp4,
+                                                                 const uint16_t* __restrict__ row_scale,
+                                                                 const float* gsc, const uint16_t* __restrict__ post_w,
+                                                                 uint16_t* __restrict__ residual) {
+  __shared__ float red[32];
+  __shared__ float yb[H];
+  float ss = 0.f;
+  for (int n = threadIdx.x; n < H; n += blockDim.x) {
+    const float pv = nvfp4 ? round_bf16(round_bf16(y[n]) * __ldg(gsc)) : round_bf16(y[n] * bf16_to_f32(row_scale[n]));
+    yb[n] = pv;
+    ss = __fadd_rn(ss, __fmul_rn(pv, pv));
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) tot += red[w];
+  const float r = rms_factor(tot, H);
+  for (int n = threadIdx.x; n < H; n += blockDim.x) {
+    const float nb = round_bf16(__fmul_rn(__fmul_rn(yb[n], r), bf16_to_f32(post_w[n])));
+    residual[n] = f32_to_bf16(__fadd_rn(bf16_to_f32(residual[n]), nb));
+  }
+}
+
+// ============================================================================ lm_head
+struct LmHeadOp {
+  static constexpr Fmt kFmt = Fmt::BF16;
+  static constexpr int kPhases = 1;
+  int rows;               // local vocab rows
+  const uint16_t* x;
+  const uint16_t* w_norm;
+  const uint16_t* wt;     // [rows, H] bf16
+  uint16_t* out;
+  Scratch* scr;
+  UnitGeom g;
+
+  __device__ int items(int) const { return rows / 8; }
+  __device__ UnitGeom geom(int) const { return g; }
+  __device__ UnitDesc unit(int, int it, int half) const {
+    UnitDesc u;
+    u.codes = reinterpret_cast<const uint8_t*>(wt + static_cast<size_t>(it) * 8 * H + half * (H / 2));
+    u.scales = nullptr;
+    u.code_stride = H * 2;
+    u.scale_stride = 0;
+    u.xoff = half * (H / 2);
+    return u;
+  }
+  __device__ uint32_t* status() const { return &scr->status; }
+  __device__ uint32_t* done_counter() const { return &scr->lm_done; }
+  __device__ bool has_final() const { return false; }
+  __device__ bool between_phases(StreamSmem&, int, uint64_t) const { return true; }
+  __device__ void final_epilogue(StreamSmem&, uint8_t*, int) const {}
+  __device__ void stage(StreamSmem& sm, uint8_t* xbuf, int, int tid) const {
+    stage_rmsnorm(x, w_norm, H, reinterpret_cast<uint16_t*>(xbuf), false, sm.scratch);
+    if (tid == 0) sm.xexp = 0;
+  }
+  __device__ void item_epilogue(StreamSmem&, int, int it, int lane, float v) const {
+    const float other = __shfl_down_sync(0xffffffffu, v, 8);
+    if (lane < 8) {
+      const float logit = round_bf16(v + other);
+      const float capped = __fmul_rn(tanhf(__fdiv_rn(logit, LOGIT_SOFTCAP)), LOGIT_SOFTCAP);
+      out[it * 8 + lane] = f32_to_bf16(capped);
+    }
+  }
+};
+
+template <Fmt F>
+struct QkvOpF : QkvOp {
+  static constexpr Fmt kFmt = F;
+};
+template <Fmt F>
+struct OprojOpF : OprojOp {
+  static constexpr Fmt kFmt = F;
+};
+
+template <class Op>
+__global__ void __launch_bounds__(kThreads, 1)
+    stream_kernel(const Op op, const StreamLayout lay, uint32_t slot_bytes, uint64_t budget_ns) {
+  stream_body(op, lay, slot_bytes, budget_ns);
+}
+
+template <class Op>
+static g4_status launch_stream(g4_ctx* ctx, const Op& op, uint32_t slot_bytes, uint32_t nslots, uint32_t x_bytes,
+                               int n_items, const char* name) {
+  const StreamLayout lay = make_layout(slot_bytes, nslots, x_bytes);
+  g4_status st = check_cuda(ctx,
+                            cudaFuncSetAttribute(stream_kernel<Op>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(lay.total)),
+                            name);
+  if (st != G4_OK) return st;
+  const int grid = n_items < ctx->sm_count ? n_items : ctx->sm_count;
+  stream_kernel<Op><<<grid, kThreads, lay.total, ctx->stream>>>(op, lay, slot_bytes, ctx->wait_budget_ns);
+  return check_cuda(ctx, cudaGetLastError(), name);
+}
+
+// ---------------------------------------------------------------------------- launchers
+g4_status launch_qkv(g4_ctx* ctx, bool full, bool nvfp4, const uint16_t* x, const uint8_t* const w[3],
+                     const uint8_t* const bs[3], const uint16_t* const rs[3], const float* const gs[3],
+                     const uint16_t* in_w, const uint16_t* qn_w, const uint16_t* kn_w, const int32_t* kv_off,
+                     const int32_t* rope_off, const uint16_t* cosT, const uint16_t* sinT, uint16_t* kcache,
+                     uint16_t* vcache, uint16_t* q_out) {
+  QkvOp op;
+  const int tp = ctx->tp_world;
+  op.D = full ? DF : DS;
+  op.nq = (full ? GF : NS * GS) / tp;
+  op.nk = full ? 1 : NS / tp;
+  op.nv = full ? 0 : NS / tp;
+  op.nvfp4 = nvfp4 ? 1 : 0;
+  op.x = x;
+  op.in_w = in_w;
+  for (int i = 0; i < 3; ++i) {
+    op.w[i] = w[i];
+    op.bs[i] = bs[i];
+    op.rs[i] = rs[i];
+    op.gs[i] = gs[i];
+  }
+  op.qn_w = qn_w;
+  op.kn_w = kn_w;
+  op.kv_off = kv_off;
+  op.rope_off = rope_off;
+  op.cosT = cosT;
+  op.sinT = sinT;
+  op.table_elems = static_cast<long long>(E) * op.D;
+  op.kc = kcache;
+  op.vc = vcache;
+  op.cache_elems = full ? static_cast<long long>(TF) * DF : static_cast<long long>(TS) * op.nk * DS;
+  op.q_out = q_out;
+  op.scr = ctx->buf.scratch;
+  op.rows = ctx->buf.rows;
+  op.g = nvfp4 ? make_geom(H / 2, H / 16, true) : make_geom(H / 2, 0, true);
+  const int n_items = nvfp4 ? (op.nq + op.nk + op.nv) * op.D / 16 : (op.nq + op.nk + op.nv) * op.D / 8;
+  if (nvfp4) {
+    QkvOpF<Fmt::NVFP4> o;
+    static_cast<QkvOp&>(o) = op;
+    return launch_stream(ctx, o, op.g.slot_bytes, 8, H * 2, n_items, "qkv_nvfp4");
+  }
+  QkvOpF<Fmt::FP8> o;
+  static_cast<QkvOp&>(o) = op;
+  return launch_stream(ctx, o, op.g.slot_bytes, 8, H * 2, n_items, "qkv_fp8");
+}
+
+g4_status launch_oproj(g4_ctx* ctx, bool full, bool nvfp4, const uint16_t* x, const float* rsum, const uint16_t* post_w,
+                       const uint8_t* w, const uint8_t* bs, const uint16_t* row_scale, const float* gsc,
+                       uint16_t* residual) {
+  OprojOp op;
+  const int tp = ctx->tp_world;
+  op.K = (full ? QF : QS) / tp;
+  op.kc = op.K >= 1024 ? 1024 : op.K;
+  if (nvfp4) op.kc = op.K >= 2048 ? 2048 : op.K;
+  op.kq = op.K / op.kc;
+  op.nvfp4 = nvfp4 ? 1 : 0;
+  op.Dh = full ? DF : 0;
+  op.x = x;
+  op.rsum = rsum;
+  op.post_w = post_w;
+  op.w = w;
+  op.bs = bs;
+  op.row_scale = row_scale;
+  op.gsc = gsc;
+  op.residual = residual;
+  op.scr = ctx->buf.scratch;
+  op.part = ctx->buf.part;
+  op.ybuf = tp > 1 ? ctx->buf.ybuf : nullptr;
+  op.g = nvfp4 ? make_geom(op.kc / 2, op.kc / 16, op.kq == 1) : make_geom(op.kc, 0, true);
+  const uint32_t xb = static_cast<uint32_t>(op.K * 2 > H * 4 ? op.K * 2 : H * 4);
+  const int n_items = (H / 8) * ((op.kq + 1) / 2);
+  g4_status st;
+  if (nvfp4) {
+    OprojOpF<Fmt::NVFP4> o;
+    static_cast<OprojOp&>(o) = op;
+    st = launch_stream(ctx, o, op.g.slot_bytes, 8, xb, n_items, "oproj_nvfp4");
+  } else {
+    OprojOpF<Fmt::FP8> o;
+    static_cast<OprojOp&>(o) = op;
+    st = launch_stream(ctx, o, op.g.slot_bytes, 8, xb, n_items, "oproj_fp8");
+  }
+  if (st != G4_OK || tp == 1) return st;
+  st = allreduce_f32(ctx, ctx->buf.ybuf, H);
+  if (st != G4_OK) return st;
+  oproj_tp_epilogue_kernel<<<1, 1024, 0, ctx->stream>>>(ctx->buf.ybuf, op.nvfp4, row_scale, gsc, post_w, residual);
+  return check_cuda(ctx, cudaGetLastError(), "oproj_tp_epilogue");
+}
+
+g4_status launch_lm_head(g4_ctx* ctx, const uint16_t* x, const uint16_t* w_norm, const uint16_t* wt, uint16_t* out) {
+  LmHeadOp op;
+  op.rows = W / ctx->tp_world;
+  op.x = x;
+  op.w_norm = w_norm;
+  op.wt = wt;
+  op.out = out;
+  op.scr = ctx->buf.scratch;
+  op.g = make_geom(H, 0, true);  // 1920 bf16 per row per unit = 3840 bytes
+  return launch_stream(ctx, op, op.g.slot_bytes, 5, H * 2, op.rows / 8, "lm_head");
+}
+
+}  // namespace g4

@@ -1,0 +1,253 @@
+/*
+ * g4.h - C ABI of the B200 (sm_100a) Gemma-4-12B text-decoder hot path.
+ *
+ * Each `g4_<op>` entry point is the drop-in for the `#[device]` function of the same
+ * name in the reference crate's `src/ops.rs`.  The reference launches those as
+ * `launch(ops::<op>, (ctx, &a, &mut b, ...)).await` (src/host/runtime.rs:316-511); here
+ * the same call is `g4_<op>(ctx, a, b, ...)` with:
+ *   - the SAME argument order as the ops.rs signature (the `ctx` first, then tensors);
+ *   - device pointers in the reference's dtypes and row-major layouts (shapes below,
+ *     named by the reference's axes, src/axes.rs: H=3840 L=15360 W=262144 Ns=8 Gs=2
+ *     Ds=256 Qs=4096 Ps=2048 Ts=1024 Gf=16 Df=512 Qf=8192 Pf=512 Tf=512 E=32768);
+ *   - `&mut` tensors written in place exactly where the reference writes them;
+ *   - offsets kept as device-resident int32 BYTE offsets (src/host/runtime.rs:213-228),
+ *     so a whole decode step can be captured in a CUDA graph and replayed;
+ *   - work issued asynchronously on the context's stream (g4_ctx_set_stream), in stream
+ *     order, like the reference's awaited launches;
+ *   - a g4_status return instead of the reference's panics.
+ *
+ * Storage formats (identical to the reference checkpoint, src/host/load.rs:10-191):
+ *   bf16   : uint16 bit patterns.
+ *   f8e4m3 : one byte per element (OCP E4M3FN).
+ *   f4e2m1 : NVFP4 codes packed two per byte, LOW nibble = even element
+ *            (scripts/fixture_prng.py:153-168), a [N, K] matrix stored as [N, K/2] bytes.
+ *   NVFP4 block scale : one f8e4m3 per 16 consecutive K elements, [N, K/16].
+ *   NVFP4 global scale: one f32, already the RECIPROCAL of the checkpoint value
+ *            (src/host/load.rs:171-191), multiplied into the projection result.
+ *
+ * Threading: one g4_ctx per host thread, like the reference's non-Send
+ * `Context::acquire()` guard (src/api/worker.rs:73-99).  Pointers must be 16-byte
+ * aligned (cudaMalloc gives 256).  Shapes are the reference's fixed axes unless an
+ * entry point says otherwise; under tensor parallelism (g4_ctx_init_tp) the weight
+ * arguments are this rank's shard, as documented per entry point.
+ */
+#ifndef G4_B200_API_H_
+#define G4_B200_API_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef uint16_t g4_bf16;   /* bfloat16 bits                                  */
+typedef uint8_t g4_f8e4m3;  /* E4M3FN byte                                    */
+typedef uint8_t g4_f4x2;    /* two E2M1 codes, low nibble = even element      */
+typedef struct CUstream_st* g4_stream_t; /* same type as cudaStream_t          */
+typedef struct g4_ctx g4_ctx;
+
+typedef enum g4_status {
+  G4_OK = 0,
+  G4_ERR_BAD_ARG = 1,     /* null/misaligned pointer, bad size or rank          */
+  G4_ERR_CUDA = 2,        /* a CUDA runtime call or kernel launch failed        */
+  G4_ERR_NCCL = 3,        /* an NCCL call failed                                */
+  G4_ERR_TIMEOUT = 4,     /* a bounded device-side wait gave up                 */
+  G4_ERR_UNSUPPORTED = 5  /* configuration not built into this library          */
+} g4_status;
+
+/* Model constants (src/lib.rs:19-22, src/axes.rs:4-29). */
+#define G4_H 3840
+#define G4_L 15360
+#define G4_W 262144
+#define G4_NS 8
+#define G4_GS 2
+#define G4_DS 256
+#define G4_QS 4096
+#define G4_PS 2048
+#define G4_TS 1024
+#define G4_GF 16
+#define G4_DF 512
+#define G4_QF 8192
+#define G4_PF 512
+#define G4_TF 512
+#define G4_E 32768
+#define G4_LAYERS 48
+
+/* ------------------------------------------------------------------------------ */
+/* Context (replaces furiosa_opt_std::Context; no reference entry point)           */
+/* ------------------------------------------------------------------------------ */
+
+/* Create a context on CUDA device `device`: allocates this context's scratch
+ * (partial sums, completion counters, intermediate activations).  Replaces
+ * `Context::acquire()` (src/api/worker.rs:85). */
+g4_status g4_ctx_create(int device, g4_ctx** out);
+g4_status g4_ctx_destroy(g4_ctx* ctx);
+/* Stream all subsequent entry points of this context are issued on (default: the
+ * legacy default stream). */
+g4_status g4_ctx_set_stream(g4_ctx* ctx, g4_stream_t stream);
+/* Tensor parallelism: this context becomes rank `rank` of `world` (1, 2, 4 or 8).
+ * `nccl_id` points to the 128-byte ncclUniqueId rank 0 created (g4_nccl_unique_id)
+ * and broadcast out of band.  After this, projection entry points take this rank's
+ * weight shard (column-parallel gate/up/q/k/v rows, row-parallel down/o K-slices)
+ * and all-reduce the row-parallel partial sums before their RMSNorm epilogue. */
+g4_status g4_nccl_unique_id(uint8_t out_id[128]);
+g4_status g4_ctx_init_tp(g4_ctx* ctx, int rank, int world, const uint8_t nccl_id[128]);
+/* Message of the last failing call on this context (never NULL). */
+const char* g4_ctx_last_error(const g4_ctx* ctx);
+/* Time limit, in microseconds, of every bounded device-side wait (mbarrier, grid-wide
+ * and cross-GPU waits inside fused kernels); default 2 s.  A wait that runs out sets a
+ * bit in the context's device status word and its kernel returns early. */
+g4_status g4_ctx_set_wait_budget(g4_ctx* ctx, uint32_t timeout_us);
+/* Synchronise the context's stream, then read and clear the device status word
+ * (0 = no kernel reported a timeout or an out-of-range device offset).  Returns
+ * G4_ERR_TIMEOUT / G4_ERR_BAD_ARG when a bit was set. */
+g4_status g4_ctx_poll_device_status(g4_ctx* ctx, uint32_t* out_bits);
+/* Library build id string ("g4b200 <version> sm_100a"). */
+const char* g4_version(void);
+
+/* ------------------------------------------------------------------------------ */
+/* Text entry points (src/ops.rs)                                                   */
+/* ------------------------------------------------------------------------------ */
+
+/* ops::embed_token (src/ops.rs:9-36): out[H] = bf16(table[row] * bf16(61.967734)),
+ * row = *offset / (H*2), `offset` a device int32 byte offset into table[W,H]. */
+g4_status g4_embed_token(g4_ctx* ctx, const g4_bf16* embedding_table, const int32_t* offset,
+                         g4_bf16* out);
+
+/* ops::copy_hidden_state (src/ops.rs:38-42): out[H] = x[H]. */
+g4_status g4_copy_hidden_state(g4_ctx* ctx, const g4_bf16* x, g4_bf16* out);
+
+/* ops::sliding_project_qkv (src/ops.rs:44-84).  Input RMSNorm; FP8 Q[Qs,H], K[Ps,H],
+ * V[Ps,H] projections with per-row bf16 scales; per-head q/k RMSNorm (weights [Ds]),
+ * unweighted v RMSNorm; RoPE (theta 1e4, full head) from cos/sin[E,Ds] rows at the
+ * byte offset *rope_offset (sin low half pre-negated, src/host/runtime.rs:271-299);
+ * q_out[Ns,Gs,Ds]; k,v scattered into the ring caches[Ts,Ns,Ds] at byte offset
+ * *kv_offset.  TP: Q/K/V rows are the rank's heads (Qs/N, Ps/N rows), caches and
+ * q_out the rank's heads. */
+g4_status g4_sliding_project_qkv(g4_ctx* ctx, const g4_bf16* x, const g4_f8e4m3* q_weight,
+                                 const g4_f8e4m3* k_weight, const g4_f8e4m3* v_weight,
+                                 const g4_bf16* q_weight_scale, const g4_bf16* k_weight_scale,
+                                 const g4_bf16* v_weight_scale, const g4_bf16* input_rms_weight,
+                                 const g4_bf16* q_rms_weight, const g4_bf16* k_rms_weight,
+                                 const int32_t* kv_offset, const int32_t* rope_offset,
+                                 const g4_bf16* cos, const g4_bf16* sin, g4_bf16* k_cache,
+                                 g4_bf16* v_cache, g4_bf16* q_out);
+
+/* ops::full_project_qkv (src/ops.rs:86-124).  Full-attention (MQA) geometry: FP8
+ * Q[Qf,H], K[Pf,H]; V = unweighted RMSNorm of the raw K projection; partial RoPE
+ * (theta 1e6, first quarter of the angles) over Df; writes q_out[Gf,Df] and one row
+ * of the page caches[Tf,Df] at byte offset *kv_offset.  TP: Q rows are the rank's
+ * heads; K/V (one head) is computed redundantly on every rank. */
+g4_status g4_full_project_qkv(g4_ctx* ctx, const g4_bf16* x, const g4_f8e4m3* q_weight,
+                              const g4_f8e4m3* k_weight, const g4_bf16* q_weight_scale,
+                              const g4_bf16* k_weight_scale, const g4_bf16* input_rms_weight,
+                              const g4_bf16* q_rms_weight, const g4_bf16* k_rms_weight,
+                              const int32_t* kv_offset, const int32_t* rope_offset,
+                              const g4_bf16* cos, const g4_bf16* sin, g4_bf16* k_cache,
+                              g4_bf16* v_cache, g4_bf16* q_out);
+
+/* ops::sliding_attention (src/ops.rs:126-136): GQA (2 q heads per kv head), scale
+ * 1.0, softmax over the ring slots whose f32 mask[Ts] is > 0, out[Ns,Gs,Ds]. */
+g4_status g4_sliding_attention(g4_ctx* ctx, const g4_bf16* q, const g4_bf16* k,
+                               const g4_bf16* v, const float* mask, g4_bf16* out);
+
+/* ops::sliding_attention_output (src/ops.rs:138-158): residual[H] +=
+ * RMSNorm(bf16(Wo[H,Qs]·x * o_scale)).  TP: Wo is the rank's K-slice [H, Qs/N]
+ * (passed with row stride Qs/N) and x the rank's heads. */
+g4_status g4_sliding_attention_output(g4_ctx* ctx, const g4_bf16* x,
+                                      const g4_bf16* post_attn_rms_weight,
+                                      const g4_f8e4m3* o_weight, const g4_bf16* o_weight_scale,
+                                      g4_bf16* residual);
+
+/* ops::full_attention_first_page (src/ops.rs:160-172): one 512-row page of MQA
+ * attention for the 16 q heads; initialises running_max[Gf], running_sum[Gf] and the
+ * UNNORMALISED out[Gf,Df] (bf16). */
+g4_status g4_full_attention_first_page(g4_ctx* ctx, const g4_bf16* q, const g4_bf16* k,
+                                       const g4_bf16* v, const float* mask, float* running_max,
+                                       float* running_sum, g4_bf16* out);
+
+/* ops::full_attention_page (src/ops.rs:174-186): online-softmax update of
+ * running_max/running_sum/out with one more page. */
+g4_status g4_full_attention_page(g4_ctx* ctx, const g4_bf16* q, const g4_bf16* k,
+                                 const g4_bf16* v, const float* mask, float* running_max,
+                                 float* running_sum, g4_bf16* out);
+
+/* ops::full_attention_output (src/ops.rs:188-211): x/running_sum per head, FP8
+ * o-proj Wo[H,Qf], RMSNorm, residual add in place.  TP: Wo is the rank's K-slice. */
+g4_status g4_full_attention_output(g4_ctx* ctx, const g4_bf16* x, const float* running_sum,
+                                   const g4_bf16* post_attn_rms_weight,
+                                   const g4_f8e4m3* o_weight, const g4_bf16* o_weight_scale,
+                                   g4_bf16* residual);
+
+/* ops::decoder_feedforward (src/ops.rs:213-253), the primary hot path:
+ *   x = RMSNorm(residual, pre_ff); h = gelu_tanh(bf16(bf16(Wg·x)*gs_g)) * bf16(bf16(Wu·x)*gs_u);
+ *   y = bf16(bf16(Wd·h)*gs_d); residual = bf16(bf16(residual + RMSNorm(y, post_ff)) * layer_scalar[0])
+ * with NVFP4 weights (packed codes + E4M3 block-16 scales + reciprocal f32 global
+ * scales), in place on residual[H].  layer_scalar is bf16 [8] (replicated,
+ * src/host/load.rs:99-111).  TP: up/gate are the rank's L/N rows ([L/N,H/2] codes,
+ * [L/N,H/16] scales), down the rank's K-slice ([H, L/N] as [H, L/(2N)] codes with
+ * row stride L/(2N), scales [H, L/(16N)]). */
+g4_status g4_decoder_feedforward(g4_ctx* ctx, g4_bf16* residual, const g4_bf16* pre_ff_rms_weight,
+                                 const g4_f4x2* up_weight_packed, const g4_f4x2* gate_weight_packed,
+                                 const g4_f4x2* down_weight_packed,
+                                 const g4_f8e4m3* up_weight_scale,
+                                 const g4_f8e4m3* gate_weight_scale,
+                                 const g4_f8e4m3* down_weight_scale, const float* up_global_scale,
+                                 const float* gate_global_scale, const float* down_global_scale,
+                                 const g4_bf16* post_ff_rms_weight, const g4_bf16* layer_scalar);
+
+/* ops::final_norm_and_logits (src/ops.rs:255-312): out[W] = bf16(tanh(l/30)*30),
+ * l = bf16(lm_head[W,H] · RMSNorm(input, rms_weight)).  TP: lm_head is the rank's
+ * vocab slice [W/N, H] and out the rank's W/N logits. */
+g4_status g4_final_norm_and_logits(g4_ctx* ctx, const g4_bf16* input, const g4_bf16* rms_weight,
+                                   const g4_bf16* lm_head_weight, g4_bf16* out);
+
+/* ------------------------------------------------------------------------------ */
+/* B200 additions (no single reference entry point; each names what it replaces)    */
+/* ------------------------------------------------------------------------------ */
+
+/* All pages of one full-attention layer in ONE split-KV launch (replaces the host loop
+ * of full_attention_first_page/_page dispatches, src/host/runtime.rs:438-459).
+ * k_pages/v_pages: DEVICE arrays of n_pages page pointers ([Tf,Df] bf16 each); rows
+ * [0, last_row] of the last page and every row of earlier pages are attended.
+ * Writes the NORMALISED output into out[Gf,Df] and 1.0 into running_sum[Gf], so
+ * g4_full_attention_output consumes it unchanged. */
+g4_status g4_full_attention_paged(g4_ctx* ctx, const g4_bf16* q, const g4_bf16* const* k_pages,
+                                  const g4_bf16* const* v_pages, int n_pages, int last_row,
+                                  float* running_sum, g4_bf16* out);
+
+/* Greedy sampling on the device (replaces the 512 KB logits read-back and host
+ * argmax of src/host/generate.rs:130-143): *out_index = first index of the maximum
+ * of logits[n] (bf16). */
+g4_status g4_argmax_bf16(g4_ctx* ctx, const g4_bf16* logits, int n, int32_t* out_index);
+
+/* Bit-exact dequantisation checks (scripts/generate_references.py:207-216,622-626):
+ * out[n,k] = bf16(e2m1(codes) * e4m3(scale[n, k/16])) and out[n,k] = bf16(e4m3(w)). */
+g4_status g4_dequant_nvfp4(g4_ctx* ctx, const g4_f4x2* packed, const g4_f8e4m3* block_scale,
+                           int rows, int cols, g4_bf16* out);
+g4_status g4_dequant_fp8(g4_ctx* ctx, const g4_f8e4m3* weight, int64_t count, g4_bf16* out);
+
+/* NVFP4 variants of the attention projections (the same GEMV
+ * engine with E2M1 codes, E4M3 block-16 scales and an f32 reciprocal global scale in
+ * place of the FP8 per-row scales).  Argument order follows the FP8 entry points with
+ * each (weight, weight_scale) pair replaced by (packed codes, block scales, global
+ * scale). */
+g4_status g4_sliding_project_qkv_nvfp4(
+    g4_ctx* ctx, const g4_bf16* x, const g4_f4x2* q_weight, const g4_f4x2* k_weight,
+    const g4_f4x2* v_weight, const g4_f8e4m3* q_block_scale, const g4_f8e4m3* k_block_scale,
+    const g4_f8e4m3* v_block_scale, const float* q_global_scale, const float* k_global_scale,
+    const float* v_global_scale, const g4_bf16* input_rms_weight, const g4_bf16* q_rms_weight,
+    const g4_bf16* k_rms_weight, const int32_t* kv_offset, const int32_t* rope_offset,
+    const g4_bf16* cos, const g4_bf16* sin, g4_bf16* k_cache, g4_bf16* v_cache, g4_bf16* q_out);
+
+g4_status g4_sliding_attention_output_nvfp4(g4_ctx* ctx, const g4_bf16* x,
+                                            const g4_bf16* post_attn_rms_weight,
+                                            const g4_f4x2* o_weight,
+                                            const g4_f8e4m3* o_block_scale,
+                                            const float* o_global_scale, g4_bf16* residual);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* G4_B200_API_H_ */
