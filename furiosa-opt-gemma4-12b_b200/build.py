@@ -61,7 +61,10 @@ def build(verbose_ptxas: bool = False, force: bool = False) -> Path:
         objs = list(ex.map(compile_one, sources))
     newest_obj = max(o.stat().st_mtime for o in objs)
     if force or not OUT.exists() or OUT.stat().st_mtime < newest_obj:
-        cmd = [cc, *ARCH, "-shared", "-o", str(OUT), *map(str, objs), "-ldl", "-Xlinker", "-z,defs"]
+        # -Bsymbolic: calls inside the library bind to its own definitions, so another
+        # library exporting the same names cannot interpose on them
+        cmd = [cc, *ARCH, "-shared", "-o", str(OUT), *map(str, objs), "-ldl", "-Xlinker", "-z,defs",
+               "-Xlinker", "-Bsymbolic"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             sys.stderr.write(res.stdout + res.stderr)

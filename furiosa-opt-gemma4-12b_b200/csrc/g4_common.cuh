@@ -189,11 +189,37 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Waits for `parity` to complete; returns false (and leaves) once `deadline_ns` passes.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t deadline_ns) {
+// Polls with the non-blocking test_wait and a short sleep, so a completed phase is seen
+// within tens of nanoseconds instead of after a suspended thread's wake-up interval.
+// Hardware-suspending wait (mbarrier.try_wait): frees the scheduler for other warps;
+// used where a slightly later wake-up does not matter (the producer).
+__device__ __forceinline__ bool mbar_wait_suspend(uint64_t* bar, uint32_t parity, uint64_t deadline_ns) {
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
-    if ((++spins & 255u) == 0u && global_ns() > deadline_ns) return false;
+    if ((++spins & 63u) == 0u && global_ns() > deadline_ns) return false;
+  }
+  return true;
+}
+// `eager` waiters never sleep (a lone latency-critical warp).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t deadline_ns,
+                                          bool eager = false) {
+  uint32_t spins = 0;
+  while (!mbar_test_wait(bar, parity)) {
+    ++spins;
+    if (!eager && spins > 64) __nanosleep(20);
+    if ((spins & 255u) == 0u && global_ns() > deadline_ns) return false;
   }
   return true;
 }

@@ -6,7 +6,7 @@
 
 #include <string>
 
-#include "../../include/g4.h"
+#include "g4.h"
 
 struct ncclComm;
 

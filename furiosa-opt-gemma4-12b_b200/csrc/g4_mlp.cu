@@ -43,11 +43,11 @@ struct MlpOp {
   uint16_t* hbuf;
   float* ybuf;      // TP: f32 partial y for the all-reduce (nullptr: fused epilogue)
   int lrows;        // local intermediate rows (L / tp)
-  int kc;           // down K per unit (3840, or lrows when smaller)
-  int kq;           // down units per row tile = lrows / kc
-  UnitGeom g0, g1;
+  int dq;           // down: K segments per row (pseudo-rows per real row)
+  UnitGeom g0, g1;  // gate/up: 8 rows x 3840 K; down: 8/dq rows x full K
 
-  __device__ int items(int ph) const { return ph == 0 ? lrows / 8 : (H / 8) * kq; }
+  __device__ int down_rows() const { return 8 / dq; }
+  __device__ int items(int ph) const { return ph == 0 ? lrows / 8 : H / down_rows(); }
   __device__ UnitGeom geom(int ph) const { return ph == 0 ? g0 : g1; }
   __device__ UnitDesc unit(int ph, int it, int half) const {
     UnitDesc u;
@@ -64,13 +64,12 @@ struct MlpOp {
         u.codes = nullptr;
         return u;
       }
-      const int r = it / kq, q = it % kq;
       const size_t cstride = lrows / 2, sstride = lrows / 16;
-      u.codes = down_p + static_cast<size_t>(r) * 8 * cstride + static_cast<size_t>(q) * (kc / 2);
-      u.scales = down_s + static_cast<size_t>(r) * 8 * sstride + static_cast<size_t>(q) * (kc / 16);
+      u.codes = down_p + static_cast<size_t>(it) * down_rows() * cstride;
+      u.scales = down_s + static_cast<size_t>(it) * down_rows() * sstride;
       u.code_stride = static_cast<uint32_t>(cstride);
       u.scale_stride = static_cast<uint32_t>(sstride);
-      u.xoff = q * kc;
+      u.xoff = 0;
     }
     return u;
   }
@@ -114,19 +113,15 @@ struct MlpOp {
       const float m = warp_max(fabsf(hv));
       if (lane == 0) atomicMax(&scr->mlp_amax, __float_as_uint(m));
     } else {
-      if (lane < 8) {
-        const int r = it / kq, q = it % kq;
-        part[q * H + r * 8 + lane] = v * unscale;
-      }
+      const float y = sum_pseudo_rows(v, lane, dq);
+      if (lane < down_rows()) part[it * down_rows() + lane] = y * unscale;
     }
   }
 
   __device__ void final_epilogue(StreamSmem& sm, uint8_t* xbuf, int tid) const {
     float* y = reinterpret_cast<float*>(xbuf);
     for (int n = tid; n < H; n += kConsumerThreads) {
-      float s = 0.f;
-      for (int q = 0; q < kq; ++q) s += __ldcg(part + q * H + n);
-      y[n] = s;
+      y[n] = __ldcg(part + n);
     }
     if (ybuf != nullptr) {
       for (int n = tid; n < H; n += kConsumerThreads) ybuf[n] = y[n];
@@ -212,13 +207,16 @@ g4_status launch_decoder_feedforward(g4_ctx* ctx, uint16_t* residual, const uint
   op.hbuf = ctx->buf.hbuf;
   op.ybuf = ctx->tp_world > 1 ? ctx->buf.ybuf : nullptr;
   op.lrows = L / ctx->tp_world;
-  op.kc = (op.lrows % 3840 == 0) ? 3840 : op.lrows;
-  op.kq = op.lrows / op.kc;
-  op.g0 = make_geom(H / 2, H / 16, true);
-  op.g1 = make_geom(op.kc / 2, op.kc / 16, op.kq == 1);
-  if (op.g1.sb % 16 != 0 && !op.g1.scale_block) return fail(ctx, G4_ERR_UNSUPPORTED, "MLP shard scale layout");
+  // down rows hold lrows K elements: cut into dq segments of 3840 (one segment when smaller)
+  op.dq = (op.lrows % 3840 == 0) ? op.lrows / 3840 : 1;
+  op.g0 = make_geom(Fmt::NVFP4, H / 2, 1);
+  op.g1 = make_geom(Fmt::NVFP4, op.lrows / 2 / op.dq, op.dq);
+  if (!geom_ok(op.g0, H / 2, H / 16) || !geom_ok(op.g1, op.lrows / 2, op.lrows / 16))
+    return fail(ctx, G4_ERR_UNSUPPORTED, "MLP shard geometry");
   const uint32_t slot_bytes = op.g0.slot_bytes > op.g1.slot_bytes ? op.g0.slot_bytes : op.g1.slot_bytes;
-  const StreamLayout lay = make_layout(slot_bytes, kMlpSlots, static_cast<uint32_t>(op.lrows > H ? op.lrows : H) * 4);
+  // activation buffer: h as f16 (phase 1) or the f32 down-projection sums (final epilogue)
+  const uint32_t x_bytes = static_cast<uint32_t>(op.lrows * 2 > H * 4 ? op.lrows * 2 : H * 4);
+  const StreamLayout lay = make_layout(slot_bytes, kMlpSlots, x_bytes);
   static bool attr_set[16] = {};
   if (!attr_set[ctx->device & 15]) {
     g4_status st = check_cuda(ctx, cudaFuncSetAttribute(mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -65,24 +65,20 @@ struct QkvOp {
       r = row - (nq + nk) * D;
     }
   }
+  // FP8: a unit is 4 rows x both K halves (2 pseudo-rows per row), an item 8 rows;
+  // NVFP4: a unit is 8 rows x full K, an item 16 rows.
+  __device__ int unit_rows() const { return nvfp4 ? 8 : 4; }
   __device__ UnitDesc unit(int, int it, int half) const {
     UnitDesc u;
-    int row0, koff;
-    if (nvfp4) {
-      row0 = it * 16 + half * 8;
-      koff = 0;
-    } else {
-      row0 = it * 8;
-      koff = half * (H / 2);
-    }
+    const int row0 = (it * 2 + half) * unit_rows();
     int m, r;
     locate(row0, m, r);
     const uint32_t rowbytes = nvfp4 ? H / 2 : H;
-    u.codes = w[m] + static_cast<size_t>(r) * rowbytes + (nvfp4 ? 0 : koff);
+    u.codes = w[m] + static_cast<size_t>(r) * rowbytes;
     u.scales = nvfp4 ? bs[m] + static_cast<size_t>(r) * (H / 16) : nullptr;
     u.code_stride = rowbytes;
     u.scale_stride = H / 16;
-    u.xoff = koff;
+    u.xoff = 0;
     return u;
   }
   __device__ uint32_t* status() const { return &scr->status; }
@@ -106,17 +102,10 @@ struct QkvOp {
 
   __device__ void item_epilogue(StreamSmem& sm, int, int it, int lane, float v) const {
     const float unscale = ldexpf(1.0f, -sm.xexp);
-    int row0, nrows;
-    if (nvfp4) {
-      row0 = it * 16;
-      nrows = 16;
-      if (lane < 16) rows[row0 + lane] = v * unscale;
-    } else {
-      row0 = it * 8;
-      nrows = 8;
-      const float other = __shfl_down_sync(0xffffffffu, v, 8);
-      if (lane < 8) rows[row0 + lane] = (v + other) * unscale;
-    }
+    const int nrows = 2 * unit_rows();
+    const int row0 = it * nrows;
+    const float rv = sum_pseudo_rows(v, lane, nvfp4 ? 1 : 2);
+    if (lane < nrows) rows[row0 + lane] = rv * unscale;
     __syncwarp();
     const int head = row0 / D;
     uint32_t old = 0;
@@ -204,8 +193,7 @@ struct QkvOp {
 struct OprojOp {
   static constexpr int kPhases = 1;
   int K;            // local input width
-  int kc;           // K per unit
-  int kq;           // units per row tile
+  int q;            // K segments per row (pseudo-rows per real row)
   int nvfp4;
   int Dh;           // head dim for the running-sum division (0: none)
   const uint16_t* x;
@@ -221,24 +209,19 @@ struct OprojOp {
   float* ybuf;      // TP: partial y (already unscaled) for the all-reduce
   UnitGeom g;
 
-  __device__ int pairs() const { return (kq + 1) / 2; }
-  __device__ int items(int) const { return (H / 8) * pairs(); }
+  // a unit is 8/q whole output rows; an item two units (A, B)
+  __device__ int unit_rows() const { return 8 / q; }
+  __device__ int items(int) const { return H / (2 * unit_rows()); }
   __device__ UnitGeom geom(int) const { return g; }
   __device__ UnitDesc unit(int, int it, int half) const {
     UnitDesc u;
-    const int r = it / pairs(), p = it % pairs();
-    const int q = 2 * p + half;
-    if (q >= kq) {
-      u.codes = nullptr;
-      return u;
-    }
+    const int row0 = (it * 2 + half) * unit_rows();
     const uint32_t rowbytes = nvfp4 ? K / 2 : K;
-    const uint32_t unitbytes = nvfp4 ? kc / 2 : kc;
-    u.codes = w + static_cast<size_t>(r) * 8 * rowbytes + static_cast<size_t>(q) * unitbytes;
-    u.scales = nvfp4 ? bs + static_cast<size_t>(r) * 8 * (K / 16) + static_cast<size_t>(q) * (kc / 16) : nullptr;
+    u.codes = w + static_cast<size_t>(row0) * rowbytes;
+    u.scales = nvfp4 ? bs + static_cast<size_t>(row0) * (K / 16) : nullptr;
     u.code_stride = rowbytes;
     u.scale_stride = K / 16;
-    u.xoff = q * kc;
+    u.xoff = 0;
     return u;
   }
   __device__ uint32_t* status() const { return &scr->status; }
@@ -262,11 +245,8 @@ struct OprojOp {
   }
 
   __device__ void item_epilogue(StreamSmem& sm, int, int it, int lane, float v) const {
-    const float other = __shfl_down_sync(0xffffffffu, v, 8);
-    if (lane < 8) {
-      const int r = it / pairs(), p = it % pairs();
-      part[p * H + r * 8 + lane] = (v + other) * ldexpf(1.0f, -sm.xexp);
-    }
+    const float rv = sum_pseudo_rows(v, lane, q);
+    if (lane < 2 * unit_rows()) part[it * 2 * unit_rows() + lane] = rv * ldexpf(1.0f, -sm.xexp);
   }
 
   __device__ float proj_value(int n, float y) const {
@@ -276,12 +256,7 @@ struct OprojOp {
 
   __device__ void final_epilogue(StreamSmem& sm, uint8_t* xbuf, int tid) const {
     float* y = reinterpret_cast<float*>(xbuf);
-    const int P = pairs();
-    for (int n = tid; n < H; n += kConsumerThreads) {
-      float s = 0.f;
-      for (int p = 0; p < P; ++p) s += __ldcg(part + p * H + n);
-      y[n] = s;
-    }
+    for (int n = tid; n < H; n += kConsumerThreads) y[n] = __ldcg(part + n);
     if (ybuf != nullptr) {
       for (int n = tid; n < H; n += kConsumerThreads) ybuf[n] = y[n];
       return;
@@ -337,15 +312,16 @@ struct LmHeadOp {
   Scratch* scr;
   UnitGeom g;
 
-  __device__ int items(int) const { return rows / 8; }
+  // a unit is 2 vocab rows x 4 K quarters (pseudo-rows), an item 4 rows
+  __device__ int items(int) const { return rows / 4; }
   __device__ UnitGeom geom(int) const { return g; }
   __device__ UnitDesc unit(int, int it, int half) const {
     UnitDesc u;
-    u.codes = reinterpret_cast<const uint8_t*>(wt + static_cast<size_t>(it) * 8 * H + half * (H / 2));
+    u.codes = reinterpret_cast<const uint8_t*>(wt + static_cast<size_t>(it * 2 + half) * 2 * H);
     u.scales = nullptr;
     u.code_stride = H * 2;
     u.scale_stride = 0;
-    u.xoff = half * (H / 2);
+    u.xoff = 0;
     return u;
   }
   __device__ uint32_t* status() const { return &scr->status; }
@@ -358,11 +334,11 @@ struct LmHeadOp {
     if (tid == 0) sm.xexp = 0;
   }
   __device__ void item_epilogue(StreamSmem&, int, int it, int lane, float v) const {
-    const float other = __shfl_down_sync(0xffffffffu, v, 8);
-    if (lane < 8) {
-      const float logit = round_bf16(v + other);
+    const float dot = sum_pseudo_rows(v, lane, 4);
+    if (lane < 4) {
+      const float logit = round_bf16(dot);
       const float capped = __fmul_rn(tanhf(__fdiv_rn(logit, LOGIT_SOFTCAP)), LOGIT_SOFTCAP);
-      out[it * 8 + lane] = f32_to_bf16(capped);
+      out[it * 4 + lane] = f32_to_bf16(capped);
     }
   }
 };
@@ -430,7 +406,8 @@ g4_status launch_qkv(g4_ctx* ctx, bool full, bool nvfp4, const uint16_t* x, cons
   op.q_out = q_out;
   op.scr = ctx->buf.scratch;
   op.rows = ctx->buf.rows;
-  op.g = nvfp4 ? make_geom(H / 2, H / 16, true) : make_geom(H / 2, 0, true);
+  op.g = nvfp4 ? make_geom(Fmt::NVFP4, H / 2, 1) : make_geom(Fmt::FP8, H / 2, 2);
+  if (!geom_ok(op.g, nvfp4 ? H / 2 : H, H / 16)) return fail(ctx, G4_ERR_UNSUPPORTED, "qkv geometry");
   const int n_items = nvfp4 ? (op.nq + op.nk + op.nv) * op.D / 16 : (op.nq + op.nk + op.nv) * op.D / 8;
   if (nvfp4) {
     QkvOpF<Fmt::NVFP4> o;
@@ -448,9 +425,7 @@ g4_status launch_oproj(g4_ctx* ctx, bool full, bool nvfp4, const uint16_t* x, co
   OprojOp op;
   const int tp = ctx->tp_world;
   op.K = (full ? QF : QS) / tp;
-  op.kc = op.K >= 1024 ? 1024 : op.K;
-  if (nvfp4) op.kc = op.K >= 2048 ? 2048 : op.K;
-  op.kq = op.K / op.kc;
+  op.q = op.K >= 4096 ? 4 : (op.K >= 2048 ? 2 : 1);
   op.nvfp4 = nvfp4 ? 1 : 0;
   op.Dh = full ? DF : 0;
   op.x = x;
@@ -464,9 +439,11 @@ g4_status launch_oproj(g4_ctx* ctx, bool full, bool nvfp4, const uint16_t* x, co
   op.scr = ctx->buf.scratch;
   op.part = ctx->buf.part;
   op.ybuf = tp > 1 ? ctx->buf.ybuf : nullptr;
-  op.g = nvfp4 ? make_geom(op.kc / 2, op.kc / 16, op.kq == 1) : make_geom(op.kc, 0, true);
+  const uint32_t rowbytes = nvfp4 ? op.K / 2 : op.K;
+  op.g = make_geom(nvfp4 ? Fmt::NVFP4 : Fmt::FP8, rowbytes / op.q, op.q);
+  if (!geom_ok(op.g, rowbytes, op.K / 16)) return fail(ctx, G4_ERR_UNSUPPORTED, "o-proj geometry");
   const uint32_t xb = static_cast<uint32_t>(op.K * 2 > H * 4 ? op.K * 2 : H * 4);
-  const int n_items = (H / 8) * ((op.kq + 1) / 2);
+  const int n_items = H / (2 * (8 / op.q));
   g4_status st;
   if (nvfp4) {
     OprojOpF<Fmt::NVFP4> o;
@@ -492,8 +469,9 @@ g4_status launch_lm_head(g4_ctx* ctx, const uint16_t* x, const uint16_t* w_norm,
   op.wt = wt;
   op.out = out;
   op.scr = ctx->buf.scratch;
-  op.g = make_geom(H, 0, true);  // 1920 bf16 per row per unit = 3840 bytes
-  return launch_stream(ctx, op, op.g.slot_bytes, 5, H * 2, op.rows / 8, "lm_head");
+  op.g = make_geom(Fmt::BF16, H * 2 / 4, 4);  // pseudo-row = 960 bf16 = 1920 bytes
+  if (!geom_ok(op.g, H * 2, 0)) return fail(ctx, G4_ERR_UNSUPPORTED, "lm_head geometry");
+  return launch_stream(ctx, op, op.g.slot_bytes, 8, H * 2, op.rows / 4, "lm_head");
 }
 
 }  // namespace g4
