@@ -16,6 +16,8 @@
 // last gate/up items of other CTAs finish, so the phase boundary costs no HBM time.
 // Under tensor parallelism the last CTA instead writes the f32 partial y, which the
 // host all-reduces before the norm epilogue kernel.
+#include <mutex>
+
 #include "g4_internal.h"
 #include "g4_stream.cuh"
 
@@ -242,3 +244,137 @@ g4_status launch_decoder_feedforward(g4_ctx* ctx, uint16_t* residual, const uint
 }
 
 }  // namespace g4
+
+// ======================================================================= no-alloc variant
+// g4_decoder_feedforward_noalloc runs mlp_kernel above with its scratch in one fixed
+// array of this translation unit instead of a context's cudaMalloc'd buffers, for hosts
+// that own all device memory and forbid a library from allocating.  Layout of the
+// array (every offset a multiple of 256 bytes):
+//   [0, 1 KiB)            Scratch counters and the device status word
+//   [1 KiB, +H*4)         f32 down-projection sums, one per output row
+//   [16 KiB, +max*2)      bf16 intermediate vector h
+namespace {
+
+constexpr size_t kNoAllocPartOff = 1024;
+constexpr size_t kNoAllocHOff = kNoAllocPartOff + static_cast<size_t>(g4::H) * 4;
+constexpr size_t kNoAllocBytes = kNoAllocHOff + static_cast<size_t>(G4_NOALLOC_MAX_INTERMEDIATE) * 2;
+static_assert(sizeof(g4::Scratch) <= kNoAllocPartOff, "counter block overflows its 1 KiB");
+static_assert(kNoAllocHOff % 256 == 0, "h must stay 256-byte aligned");
+static_assert(kNoAllocBytes == G4_NOALLOC_SCRATCH_BYTES, "header states the array size");
+
+// In host code this name only identifies the array; its device address comes from
+// cudaGetSymbolAddress on each device.
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+struct NoAllocDevice {
+  std::once_flag once;
+  cudaError_t err = cudaSuccess;
+  const char* what = "";
+  unsigned char* base = nullptr;  // this device's address of g_noalloc_scratch
+  int sm_count = 0;
+  int smem_optin = 0;
+  bool coop = false;
+};
+constexpr int kNoAllocMaxDevices = 64;
+NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
+
+// Once per device, with that device current.  Allocates nothing: the array belongs to
+// the module image the runtime loaded on this device.
+void noalloc_setup(NoAllocDevice& d, int dev) {
+  void* ptr = nullptr;
+  cudaError_t e = cudaGetSymbolAddress((void**)&ptr, g_noalloc_scratch);
+  if (e != cudaSuccess) {
+    d.err = e;
+    d.what = "cudaGetSymbolAddress(g_noalloc_scratch)";
+    return;
+  }
+  int coop = 0;
+  if ((e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
+      (e = cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess ||
+      (e = cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev)) != cudaSuccess) {
+    d.err = e;
+    d.what = "cudaDeviceGetAttribute";
+    return;
+  }
+  d.coop = coop != 0;
+  d.base = static_cast<unsigned char*>(ptr);
+}
+
+bool noalloc_aligned(const void* p, uintptr_t a) {
+  return p != nullptr && reinterpret_cast<uintptr_t>(p) % a == 0;
+}
+
+}  // namespace
+
+extern "C" g4_status g4_decoder_feedforward_noalloc(
+    g4_stream_t stream, uint32_t intermediate_size, g4_bf16* residual, const g4_bf16* pre_ff_rms_weight,
+    const g4_f4x2* up_weight_packed, const g4_f4x2* gate_weight_packed, const g4_f4x2* down_weight_packed,
+    const g4_f8e4m3* up_weight_scale, const g4_f8e4m3* gate_weight_scale, const g4_f8e4m3* down_weight_scale,
+    const float* up_global_scale, const float* gate_global_scale, const float* down_global_scale,
+    const g4_bf16* post_ff_rms_weight, const g4_bf16* layer_scalar) {
+  using namespace g4;
+  // sizes first: nothing below runs for a call that the scratch array cannot hold
+  const uint32_t n = intermediate_size;
+  if (n > G4_NOALLOC_MAX_INTERMEDIATE) return G4_ERR_TOO_LARGE;
+  if (n == 0) return G4_ERR_BAD_ARG;
+  const uint32_t dq = (n % 3840u == 0u) ? n / 3840u : 1u;
+  MlpOp op;
+  op.lrows = static_cast<int>(n);
+  op.dq = static_cast<int>(dq);
+  op.g0 = make_geom(Fmt::NVFP4, H / 2, 1);
+  op.g1 = make_geom(Fmt::NVFP4, n / 2u / dq, dq);
+  if (n % 128u != 0u || !geom_ok(op.g0, H / 2, H / 16) || !geom_ok(op.g1, n / 2u, n / 16u))
+    return G4_ERR_UNSUPPORTED;
+  const void* p16[] = {residual, pre_ff_rms_weight, up_weight_packed, gate_weight_packed, down_weight_packed,
+                       up_weight_scale, gate_weight_scale, down_weight_scale, post_ff_rms_weight, layer_scalar};
+  for (const void* p : p16)
+    if (!noalloc_aligned(p, 16)) return G4_ERR_BAD_ARG;
+  const void* p4[] = {up_global_scale, gate_global_scale, down_global_scale};
+  for (const void* p : p4)
+    if (!noalloc_aligned(p, 4)) return G4_ERR_BAD_ARG;
+
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return G4_ERR_CUDA;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return G4_ERR_UNSUPPORTED;
+  NoAllocDevice& d = g_noalloc_dev[dev];
+  std::call_once(d.once, noalloc_setup, std::ref(d), dev);
+  if (d.err != cudaSuccess || d.base == nullptr) return G4_ERR_CUDA;
+  if (!d.coop) return G4_ERR_UNSUPPORTED;
+
+  const uint32_t slot_bytes = op.g0.slot_bytes > op.g1.slot_bytes ? op.g0.slot_bytes : op.g1.slot_bytes;
+  const uint32_t x_bytes = (n * 2u > static_cast<uint32_t>(H) * 4u) ? n * 2u : static_cast<uint32_t>(H) * 4u;
+  const StreamLayout lay = make_layout(slot_bytes, kMlpSlots, x_bytes);
+  if (lay.total > static_cast<uint32_t>(d.smem_optin)) return G4_ERR_UNSUPPORTED;
+
+  op.residual = residual;
+  op.pre_w = pre_ff_rms_weight;
+  op.post_w = post_ff_rms_weight;
+  op.layer_scalar = layer_scalar;
+  op.up_p = up_weight_packed;
+  op.gate_p = gate_weight_packed;
+  op.down_p = down_weight_packed;
+  op.up_s = up_weight_scale;
+  op.gate_s = gate_weight_scale;
+  op.down_s = down_weight_scale;
+  op.up_gs = up_global_scale;
+  op.gate_gs = gate_global_scale;
+  op.down_gs = down_global_scale;
+  op.scr = reinterpret_cast<Scratch*>(d.base);
+  op.part = reinterpret_cast<float*>(d.base + kNoAllocPartOff);
+  op.hbuf = reinterpret_cast<uint16_t*>(d.base + kNoAllocHOff);
+  op.ybuf = nullptr;
+
+  // The opt-in maximum, never lower: the context path sets this attribute once per
+  // device for its own (possibly larger) layout and must keep working after us.
+  if (cudaFuncSetAttribute(mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, d.smem_optin) != cudaSuccess)
+    return G4_ERR_CUDA;
+  // The counters and status word must start at zero; a call that gave up on a device
+  // wait may have left them set.
+  if (cudaMemsetAsync(d.base, 0, sizeof(Scratch), stream) != cudaSuccess) return G4_ERR_CUDA;
+  const uint64_t budget = 2000000000ull;  // the context default: 2 s per device-side wait
+  void* args[] = {(void*)&op, (void*)&lay, (void*)&slot_bytes, (void*)&budget};
+  if (cudaLaunchCooperativeKernel((const void*)mlp_kernel, dim3(d.sm_count), dim3(kThreads), args, lay.total,
+                                  stream) != cudaSuccess)
+    return G4_ERR_CUDA;
+  return G4_OK;
+}

@@ -25,6 +25,7 @@ __all__ = [
     "full_attention_page", "full_attention_output", "decoder_feedforward",
     "final_norm_and_logits", "full_attention_paged", "argmax_bf16", "dequant_nvfp4",
     "dequant_fp8", "sliding_project_qkv_nvfp4", "sliding_attention_output_nvfp4",
+    "decoder_feedforward_noalloc", "NOALLOC_MAX_INTERMEDIATE",
 ]
 
 H, L, W = 3840, 15360, 262144
@@ -34,7 +35,8 @@ GF, DF, QF, PF, TF, E = 16, 512, 8192, 512, 512, 32768
 _HERE = Path(__file__).resolve().parent
 _HEADER = _HERE.parent.parent / "include" / "g4.h"
 
-STATUS = {0: "OK", 1: "BAD_ARG", 2: "CUDA", 3: "NCCL", 4: "TIMEOUT", 5: "UNSUPPORTED"}
+STATUS = {0: "OK", 1: "BAD_ARG", 2: "CUDA", 3: "NCCL", 4: "TIMEOUT", 5: "UNSUPPORTED", 6: "TOO_LARGE"}
+NOALLOC_MAX_INTERMEDIATE = 15360  # G4_NOALLOC_MAX_INTERMEDIATE
 
 
 class G4Error(RuntimeError):
@@ -193,6 +195,8 @@ LIB.g4_full_attention_paged.argtypes = [_vp, _vp, _vp, _vp, _i32, _i32, _vp, _vp
 LIB.g4_argmax_bf16.argtypes = [_vp, _vp, _i32, _vp]
 LIB.g4_dequant_nvfp4.argtypes = [_vp, _vp, _vp, _i32, _i32, _vp]
 LIB.g4_dequant_fp8.argtypes = [_vp, _vp, _i64, _vp]
+LIB.g4_decoder_feedforward_noalloc.argtypes = [_vp, _u32] + [_vp] * 13
+LIB.g4_decoder_feedforward_noalloc.restype = _i32
 
 
 def _t():
@@ -441,3 +445,48 @@ def dequant_nvfp4(ctx: Context, packed, block_scale, rows: int, cols: int, out) 
 
 def dequant_fp8(ctx: Context, weight, out) -> None:
     ctx._check("g4_dequant_fp8", LIB.g4_dequant_fp8(ctx.handle, _ptr(weight), weight.numel(), _ptr(out)))
+
+
+def decoder_feedforward_noalloc(residual, pre_ff_rms_weight, up_weight_packed, gate_weight_packed,
+                                down_weight_packed, up_weight_scale, gate_weight_scale, down_weight_scale,
+                                up_global_scale, gate_global_scale, down_global_scale, post_ff_rms_weight,
+                                layer_scalar, stream=None):
+    """decoder_feedforward without a Context, for hosts where this library may not allocate
+    device memory (g4_decoder_feedforward_noalloc; no counterpart in the reference).
+
+    Same math and kernel as `decoder_feedforward`, in place on `residual`.  The
+    intermediate size n is read from `gate_weight_packed` ([n, H/2] codes); n may be at
+    most NOALLOC_MAX_INTERMEDIATE.  Scratch lives in one fixed device array per GPU that
+    every call shares, so calls must not overlap on the GPU.  Runs on `stream` (default:
+    torch's current stream of residual's device).
+    """
+    t = _t()
+    bf, u8, f8, f32 = (t.bfloat16,), (t.uint8,), (t.uint8, t.float8_e4m3fn), (t.float32,)
+    _expect("gate_weight_packed", gate_weight_packed, None, u8)
+    if gate_weight_packed.numel() % (H // 2):
+        raise ValueError(f"gate_weight_packed: {gate_weight_packed.numel()} bytes is not [n, {H // 2}]")
+    n = gate_weight_packed.numel() // (H // 2)
+    _expect("residual", residual, H, bf)
+    _expect("pre_ff_rms_weight", pre_ff_rms_weight, H, bf)
+    _expect("up_weight_packed", up_weight_packed, n * H // 2, u8)
+    _expect("down_weight_packed", down_weight_packed, H * n // 2, u8)
+    _expect("up_weight_scale", up_weight_scale, n * H // 16, f8)
+    _expect("gate_weight_scale", gate_weight_scale, n * H // 16, f8)
+    _expect("down_weight_scale", down_weight_scale, H * n // 16, f8)
+    _expect("up_global_scale", up_global_scale, 1, f32)
+    _expect("gate_global_scale", gate_global_scale, 1, f32)
+    _expect("down_global_scale", down_global_scale, 1, f32)
+    _expect("post_ff_rms_weight", post_ff_rms_weight, H, bf)
+    _expect("layer_scalar", layer_scalar, 8, bf)
+    with t.cuda.device(residual.device):
+        s = stream if stream is not None else t.cuda.current_stream()
+        code = LIB.g4_decoder_feedforward_noalloc(
+            s.cuda_stream, n, *[_ptr(a) for a in (
+                residual, pre_ff_rms_weight, up_weight_packed, gate_weight_packed, down_weight_packed,
+                up_weight_scale, gate_weight_scale, down_weight_scale, up_global_scale, gate_global_scale,
+                down_global_scale, post_ff_rms_weight, layer_scalar)])
+    if code != 0:
+        why = {6: f"intermediate size {n} exceeds the fixed scratch limit of {NOALLOC_MAX_INTERMEDIATE} rows",
+               5: f"intermediate size {n} is not 15360, 7680 or a multiple of 128 up to 3840",
+               1: "a pointer is null or misaligned"}.get(code, "a CUDA call failed")
+        raise G4Error("g4_decoder_feedforward_noalloc", code, why)

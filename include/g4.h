@@ -52,7 +52,8 @@ typedef enum g4_status {
   G4_ERR_CUDA = 2,        /* a CUDA runtime call or kernel launch failed        */
   G4_ERR_NCCL = 3,        /* an NCCL call failed                                */
   G4_ERR_TIMEOUT = 4,     /* a bounded device-side wait gave up                 */
-  G4_ERR_UNSUPPORTED = 5  /* configuration not built into this library          */
+  G4_ERR_UNSUPPORTED = 5, /* configuration not built into this library          */
+  G4_ERR_TOO_LARGE = 6    /* a size exceeds a fixed limit (no-alloc entry point) */
 } g4_status;
 
 /* Model constants (src/lib.rs:19-22, src/axes.rs:4-29). */
@@ -245,6 +246,50 @@ g4_status g4_sliding_attention_output_nvfp4(g4_ctx* ctx, const g4_bf16* x,
                                             const g4_f4x2* o_weight,
                                             const g4_f8e4m3* o_block_scale,
                                             const float* o_global_scale, g4_bf16* residual);
+
+/* ------------------------------------------------------------------------------ */
+/* Allocation-free decoder_feedforward (no counterpart in the reference)            */
+/* ------------------------------------------------------------------------------ */
+
+/* Scratch this entry point owns: one fixed array in the library's device image, on
+ * every GPU that loads the library, held until the process exits. */
+#define G4_NOALLOC_MAX_INTERMEDIATE 15360 /* rows of up/gate = K of down       */
+#define G4_NOALLOC_SCRATCH_BYTES 47104    /* 46 KiB: 1 KiB counters, f32 [H], bf16 [max intermediate] */
+
+/* The decoder_feedforward math of g4_decoder_feedforward (same formula, same kernel,
+ * in place on residual[H]) for callers that cannot allocate device memory.  It has no
+ * counterpart in the reference.  A g4_ctx needs cudaMalloc for its scratch, which some
+ * hosts do not allow: serving engines that hand every free byte of HBM to their own
+ * pool at start-up (a later cudaMalloc fails or fragments that pool), plugin hooks that
+ * must not allocate on the per-call path, and latency-critical loops that cannot take
+ * the device-wide synchronisation a cudaMalloc/cudaFree may cause.  This entry point
+ * instead keeps its scratch (counters, the down-projection sums and the intermediate
+ * vector h) in the fixed array above and calls no allocating routine.
+ *
+ *   stream            : a stream of the CURRENT device (NULL = its default stream).
+ *   intermediate_size : rows of up/gate and K of down.  G4_L for the model's layer;
+ *                       also 7680, or a multiple of 128 up to 3840 (single-GPU only,
+ *                       no all-reduce).  > G4_NOALLOC_MAX_INTERMEDIATE returns
+ *                       G4_ERR_TOO_LARGE; other shapes return G4_ERR_UNSUPPORTED.
+ *   weights           : as g4_decoder_feedforward with L = intermediate_size
+ *                       (up/gate [n, H/2] codes, [n, H/16] scales; down [H, n/2] codes,
+ *                       [H, n/16] scales).
+ *
+ * The first call on a device sets up that device (looks up the array's device address,
+ * the SM count and the launch limits); make that first call before any stream capture
+ * starts.  Every call on a device shares the one array and leaves its contents behind;
+ * each call first clears, on `stream`, the counter block that must start at zero.
+ * Calls that can overlap on the GPU (different streams without ordering between them,
+ * or different host threads) race on the array and give wrong results: order them.
+ * Device-side wait timeouts are not reported here (there is no context to poll). */
+g4_status g4_decoder_feedforward_noalloc(
+    g4_stream_t stream, uint32_t intermediate_size, g4_bf16* residual,
+    const g4_bf16* pre_ff_rms_weight, const g4_f4x2* up_weight_packed,
+    const g4_f4x2* gate_weight_packed, const g4_f4x2* down_weight_packed,
+    const g4_f8e4m3* up_weight_scale, const g4_f8e4m3* gate_weight_scale,
+    const g4_f8e4m3* down_weight_scale, const float* up_global_scale,
+    const float* gate_global_scale, const float* down_global_scale,
+    const g4_bf16* post_ff_rms_weight, const g4_bf16* layer_scalar);
 
 #ifdef __cplusplus
 }
