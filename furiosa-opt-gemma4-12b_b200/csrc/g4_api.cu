@@ -293,8 +293,7 @@ g4_status g4_sliding_attention_output(g4_ctx* ctx, const g4_bf16* x, const g4_bf
                                       const g4_f8e4m3* o_weight, const g4_bf16* o_weight_scale,
                                       g4_bf16* residual) {
   G4_CHECK_CTX(ctx);
-  G4_REQUIRE_PTRS(ctx, x, post_attn_rms_weight, o_weight, residual);
-  G4_REQUIRE_SCALARS(ctx, o_weight_scale);
+  G4_REQUIRE_PTRS(ctx, x, post_attn_rms_weight, o_weight, o_weight_scale, residual);
   return launch_oproj(ctx, false, false, x, nullptr, post_attn_rms_weight, o_weight, nullptr, o_weight_scale, nullptr,
                       residual);
 }
@@ -340,8 +339,8 @@ g4_status g4_full_attention_output(g4_ctx* ctx, const g4_bf16* x, const float* r
                                    const g4_bf16* post_attn_rms_weight, const g4_f8e4m3* o_weight,
                                    const g4_bf16* o_weight_scale, g4_bf16* residual) {
   G4_CHECK_CTX(ctx);
-  G4_REQUIRE_PTRS(ctx, x, post_attn_rms_weight, o_weight, residual);
-  G4_REQUIRE_SCALARS(ctx, running_sum, o_weight_scale);
+  G4_REQUIRE_PTRS(ctx, x, post_attn_rms_weight, o_weight, o_weight_scale, residual);
+  G4_REQUIRE_SCALARS(ctx, running_sum);
   return launch_oproj(ctx, true, false, x, running_sum, post_attn_rms_weight, o_weight, nullptr, o_weight_scale,
                       nullptr, residual);
 }

@@ -252,6 +252,14 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// Release-ordered add whose result is not needed: no round trip to wait for.
+__device__ __forceinline__ void red_add_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Pull one 128-byte line into L2 and keep it there ahead of streamed (evict-first) data.
+__device__ __forceinline__ void prefetch_l2_keep(const void* p) {
+  asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p));
+}
 __device__ __forceinline__ uint32_t atom_add_release_gpu(uint32_t* p, uint32_t v) {
   uint32_t old;
   asm volatile("atom.add.release.gpu.global.u32 %0, [%1], %2;"

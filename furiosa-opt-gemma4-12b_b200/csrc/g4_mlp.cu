@@ -7,8 +7,9 @@
 //                     (mlp.rs:13-155 projection, :218-334 GeGLU; tanh per the oracle)
 //   grid wait:        every CTA's h rows are visible (bounded spin, error flag on timeout)
 //   phase 1  stage:   h as scaled f16 (max |h| gathered with atomicMax in phase 0)
-//   phase 1  items:   8 down rows x 3840-wide K quarter each (mlp.rs:339-437), partial
-//                     sums to scratch
+//   phase 1  items:   two units of 8/dq whole down rows, each row cut into dq K segments
+//                     (TP1: 2 rows x 4 segments of 3840 per unit, 4 rows per item;
+//                     mlp.rs:339-437); one f32 sum per row to scratch
 //   final (last CTA): y = bf16(bf16(sum)*gs_d); residual = bf16(bf16(residual +
 //                     RMSNorm(y, post_ff)) * layer_scalar)   (ops.rs:248-252, residual.rs)
 //
@@ -48,8 +49,9 @@ struct MlpOp {
   int dq;           // down: K segments per row (pseudo-rows per real row)
   UnitGeom g0, g1;  // gate/up: 8 rows x 3840 K; down: 8/dq rows x full K
 
+  // down: a unit is 8/dq whole rows, an item two units (A, B) = 16/dq rows
   __device__ int down_rows() const { return 8 / dq; }
-  __device__ int items(int ph) const { return ph == 0 ? lrows / 8 : H / down_rows(); }
+  __device__ int items(int ph) const { return ph == 0 ? lrows / 8 : H / (2 * down_rows()); }
   __device__ UnitGeom geom(int ph) const { return ph == 0 ? g0 : g1; }
   __device__ UnitDesc unit(int ph, int it, int half) const {
     UnitDesc u;
@@ -60,39 +62,67 @@ struct MlpOp {
       u.scales = s + static_cast<size_t>(it) * 8 * (H / 16);
       u.code_stride = H / 2;
       u.scale_stride = H / 16;
-      u.xoff = 0;
     } else {
-      if (half) {
-        u.codes = nullptr;
-        return u;
-      }
       const size_t cstride = lrows / 2, sstride = lrows / 16;
-      u.codes = down_p + static_cast<size_t>(it) * down_rows() * cstride;
-      u.scales = down_s + static_cast<size_t>(it) * down_rows() * sstride;
+      const size_t row0 = static_cast<size_t>(2 * it + half) * down_rows();
+      u.codes = down_p + row0 * cstride;
+      u.scales = down_s + row0 * sstride;
       u.code_stride = static_cast<uint32_t>(cstride);
       u.scale_stride = static_cast<uint32_t>(sstride);
-      u.xoff = 0;
     }
     return u;
   }
   __device__ uint32_t* status() const { return &scr->status; }
   __device__ uint32_t* done_counter() const { return &scr->mlp_done; }
+  // The fused tail reads post_w, layer_scalar and down_gs once, in the last CTA: CTA c
+  // pulls line c of post_w (and CTA 0 the scalars) into L2 at kernel start.
+  __device__ void prefetch_tail(int cta, int lane) const {
+    if (ybuf != nullptr) return;  // TP: the tail runs in its own kernel after the all-reduce
+    constexpr int kBytes = H * 2, kLines = kBytes / 128 + 1;
+    const uint8_t* pw = reinterpret_cast<const uint8_t*>(post_w);
+    if (lane == 0 && cta < kLines) prefetch_l2_keep(pw + min(cta * 128, kBytes - 1));
+    if (lane == 1 && cta == 0) {
+      prefetch_l2_keep(layer_scalar);
+      prefetch_l2_keep(down_gs);
+    }
+  }
   __device__ bool has_final() const { return true; }
 
-  __device__ void stage(StreamSmem& sm, uint8_t* xbuf, int ph, int tid) const {
+  __device__ void stage(StreamSmem& sm, uint8_t* xbuf, int ph, int tid, const XLayout& xl) const {
     uint16_t* xs = reinterpret_cast<uint16_t*>(xbuf);
     if (ph == 0) {
-      const int e = stage_rmsnorm(residual, pre_w, H, xs, true, sm.scratch);
+      const int e = stage_rmsnorm(residual, pre_w, H, xs, true, sm.scratch, xl);
       if (tid == 0) {
         sm.xexp = e;
         sm.scratch[40] = __ldg(gate_gs);
         sm.scratch[41] = __ldg(up_gs);
       }
     } else {
-      const float amax = __uint_as_float(ld_acquire_gpu(&scr->mlp_amax));
+      // h and its max were published before the grid barrier (acquired by its thread 0,
+      // then bar.sync): plain L2 loads, 8 h values per 16-byte load, all issued together.
+      constexpr int kG = 4;  // lrows <= kG * 8 * kConsumerThreads
+      uint4 hv[kG];
+#pragma unroll
+      for (int k = 0; k < kG; ++k) {
+        const int gi = tid + k * kConsumerThreads;
+        if (gi * 8 < lrows) hv[k] = __ldcg(reinterpret_cast<const uint4*>(hbuf) + gi);
+      }
+      const float amax = __uint_as_float(__ldcg(&scr->mlp_amax));
       const int e = f16_scale_exponent(amax);
       const float sc = ldexpf(1.0f, e);
-      for (int i = tid; i < lrows; i += kConsumerThreads) xs[i] = f32_to_f16(bf16_to_f32(__ldcg(hbuf + i)) * sc);
+#pragma unroll
+      for (int k = 0; k < kG; ++k) {
+        const int gi = tid + k * kConsumerThreads;
+        if (gi * 8 < lrows) {
+          const uint32_t w[4] = {hv[k].x, hv[k].y, hv[k].z, hv[k].w};
+          uint32_t o[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            o[i] = pack_u16x2(f32_to_f16(bf16_to_f32(static_cast<uint16_t>(w[i] & 0xFFFFu)) * sc),
+                              f32_to_f16(bf16_to_f32(static_cast<uint16_t>(w[i] >> 16)) * sc));
+          *reinterpret_cast<uint4*>(xs + x_pos(static_cast<uint32_t>(gi) * 8u, xl)) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
       if (tid == 0) sm.xexp = e;
     }
   }
@@ -116,31 +146,61 @@ struct MlpOp {
       if (lane == 0) atomicMax(&scr->mlp_amax, __float_as_uint(m));
     } else {
       const float y = sum_pseudo_rows(v, lane, dq);
-      if (lane < down_rows()) part[it * down_rows() + lane] = y * unscale;
+      if (lane < 2 * down_rows()) part[it * 2 * down_rows() + lane] = y * unscale;
     }
   }
 
-  __device__ void final_epilogue(StreamSmem& sm, uint8_t* xbuf, int tid) const {
-    float* y = reinterpret_cast<float*>(xbuf);
-    for (int n = tid; n < H; n += kConsumerThreads) {
-      y[n] = __ldcg(part + n);
+  // Thread tid < H/8 owns outputs [8*tid, 8*tid + 8): it issues all of its loads (the
+  // down sums, the residual, the post-FF norm weight) before any math, so the tail of
+  // the launch pays one memory latency, not one per output.
+  __device__ void final_epilogue(StreamSmem& sm, uint8_t*, int tid) const {
+    const bool mine = tid < H / 8;
+    float y[8];
+    uint4 rv = make_uint4(0u, 0u, 0u, 0u), wv = rv;
+    if (mine) {
+      const float4 p0 = __ldcg(reinterpret_cast<const float4*>(part) + 2 * tid);
+      const float4 p1 = __ldcg(reinterpret_cast<const float4*>(part) + 2 * tid + 1);
+      y[0] = p0.x, y[1] = p0.y, y[2] = p0.z, y[3] = p0.w, y[4] = p1.x, y[5] = p1.y, y[6] = p1.z, y[7] = p1.w;
+      if (ybuf == nullptr) {
+        rv = *reinterpret_cast<const uint4*>(residual + 8 * tid);
+        wv = __ldg(reinterpret_cast<const uint4*>(post_w) + tid);
+      }
     }
     if (ybuf != nullptr) {
-      for (int n = tid; n < H; n += kConsumerThreads) ybuf[n] = y[n];
+      if (mine) {
+        reinterpret_cast<float4*>(ybuf)[2 * tid] = make_float4(y[0], y[1], y[2], y[3]);
+        reinterpret_cast<float4*>(ybuf)[2 * tid + 1] = make_float4(y[4], y[5], y[6], y[7]);
+      }
     } else {
       const float gsd = __ldg(down_gs);
       float ss = 0.f;
-      for (int n = tid; n < H; n += kConsumerThreads) {
-        const float d2 = round_bf16(round_bf16(y[n]) * gsd);
-        y[n] = d2;
-        ss = __fadd_rn(ss, __fmul_rn(d2, d2));
+      if (mine) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float d2 = round_bf16(round_bf16(y[i]) * gsd);
+          y[i] = d2;
+          ss = __fadd_rn(ss, __fmul_rn(d2, d2));
+        }
       }
       const float r = rms_factor(consumer_sum(ss, sm.scratch), H);
       const float ls = bf16_to_f32(layer_scalar[0]);
-      for (int n = tid; n < H; n += kConsumerThreads) {
-        const float nb = round_bf16(__fmul_rn(__fmul_rn(y[n], r), bf16_to_f32(post_w[n])));
-        const float r2 = round_bf16(__fadd_rn(bf16_to_f32(residual[n]), nb));
-        residual[n] = f32_to_bf16(__fmul_rn(r2, ls));
+      if (mine) {
+        const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          uint16_t h2[2];
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const float res = bf16_to_f32(static_cast<uint16_t>(j ? rw[i] >> 16 : rw[i] & 0xFFFFu));
+            const float pw = bf16_to_f32(static_cast<uint16_t>(j ? ww[i] >> 16 : ww[i] & 0xFFFFu));
+            const float nb = round_bf16(__fmul_rn(__fmul_rn(y[2 * i + j], r), pw));
+            const float r2 = round_bf16(__fadd_rn(res, nb));
+            h2[j] = f32_to_bf16(__fmul_rn(r2, ls));
+          }
+          o[i] = pack_u16x2(h2[0], h2[1]);
+        }
+        *reinterpret_cast<uint4*>(residual + 8 * tid) = make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
     if (tid == 0) {

@@ -78,7 +78,6 @@ struct QkvOp {
     u.scales = nvfp4 ? bs[m] + static_cast<size_t>(r) * (H / 16) : nullptr;
     u.code_stride = rowbytes;
     u.scale_stride = H / 16;
-    u.xoff = 0;
     return u;
   }
   __device__ uint32_t* status() const { return &scr->status; }
@@ -86,8 +85,9 @@ struct QkvOp {
   __device__ bool has_final() const { return false; }
   __device__ bool between_phases(StreamSmem&, int, uint64_t) const { return true; }
   __device__ void final_epilogue(StreamSmem&, uint8_t*, int) const {}
-  __device__ void stage(StreamSmem& sm, uint8_t* xbuf, int, int tid) const {
-    const int e = stage_rmsnorm(x, in_w, H, reinterpret_cast<uint16_t*>(xbuf), true, sm.scratch);
+  __device__ void prefetch_tail(int, int) const {}
+  __device__ void stage(StreamSmem& sm, uint8_t* xbuf, int, int tid, const XLayout& xl) const {
+    const int e = stage_rmsnorm(x, in_w, H, reinterpret_cast<uint16_t*>(xbuf), true, sm.scratch, xl);
     if (tid == 0) sm.xexp = e;
   }
 
@@ -221,26 +221,67 @@ struct OprojOp {
     u.scales = nvfp4 ? bs + static_cast<size_t>(row0) * (K / 16) : nullptr;
     u.code_stride = rowbytes;
     u.scale_stride = K / 16;
-    u.xoff = 0;
     return u;
   }
   __device__ uint32_t* status() const { return &scr->status; }
   __device__ uint32_t* done_counter() const { return &scr->proj_done; }
+  // The fused tail (last CTA) reads residual, post_w and the row scales: CTA c pulls line
+  // c of each into L2 at kernel start.
+  __device__ void prefetch_tail(int cta, int lane) const {
+    if (ybuf != nullptr) return;  // TP: the tail runs in its own kernel after the all-reduce
+    constexpr int kBytes = H * 2, kLines = kBytes / 128 + 1;
+    if (cta >= kLines) return;
+    const int off = min(cta * 128, kBytes - 1);
+    if (lane == 0) prefetch_l2_keep(reinterpret_cast<const uint8_t*>(post_w) + off);
+    if (lane == 1) prefetch_l2_keep(reinterpret_cast<const uint8_t*>(residual) + off);
+    if (lane == 2 && !nvfp4) prefetch_l2_keep(reinterpret_cast<const uint8_t*>(row_scale) + off);
+    if (lane == 3 && nvfp4 && cta == 0) prefetch_l2_keep(gsc);
+  }
   __device__ bool has_final() const { return true; }
   __device__ bool between_phases(StreamSmem&, int, uint64_t) const { return true; }
 
-  __device__ void stage(StreamSmem& sm, uint8_t* xbuf, int, int tid) const {
+  // 8 inputs per 16-byte load, all loads issued first (K <= kG * 8 * kConsumerThreads).
+  __device__ void stage(StreamSmem& sm, uint8_t* xbuf, int, int tid, const XLayout& xl) const {
     uint16_t* xs = reinterpret_cast<uint16_t*>(xbuf);
+    constexpr int kG = 2;
+    uint4 xv[kG];
+    float rs[kG];
+#pragma unroll
+    for (int k = 0; k < kG; ++k) {
+      const int gi = tid + k * kConsumerThreads;
+      if (gi * 8 < K) {
+        xv[k] = __ldg(reinterpret_cast<const uint4*>(x) + gi);
+        rs[k] = (Dh > 0) ? __ldg(rsum + gi * 8 / Dh) : 1.0f;  // 8 | Dh: one head per group
+      }
+    }
+    float v[kG][8];
     float amax = 0.f;
-    for (int i = tid; i < K; i += kConsumerThreads) {
-      float v = bf16_to_f32(x[i]);
-      if (Dh > 0) v = round_bf16(__fdiv_rn(v, __ldg(rsum + i / Dh)));
-      xs[i] = f32_to_bf16(v);
-      amax = fmaxf(amax, fabsf(v));
+#pragma unroll
+    for (int k = 0; k < kG; ++k) {
+      const int gi = tid + k * kConsumerThreads;
+      if (gi * 8 < K) {
+        const uint32_t w[4] = {xv[k].x, xv[k].y, xv[k].z, xv[k].w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float f = bf16_to_f32(static_cast<uint16_t>((i & 1) ? w[i >> 1] >> 16 : w[i >> 1] & 0xFFFFu));
+          if (Dh > 0) f = round_bf16(__fdiv_rn(f, rs[k]));
+          v[k][i] = f;
+          amax = fmaxf(amax, fabsf(f));
+        }
+      }
     }
     const int e = f16_scale_exponent(consumer_max(amax, sm.scratch + 32));
     const float sc = ldexpf(1.0f, e);
-    for (int i = tid; i < K; i += kConsumerThreads) xs[i] = f32_to_f16(bf16_to_f32(xs[i]) * sc);
+#pragma unroll
+    for (int k = 0; k < kG; ++k) {
+      const int gi = tid + k * kConsumerThreads;
+      if (gi * 8 < K) {
+        uint32_t o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = pack_u16x2(f32_to_f16(v[k][2 * i] * sc), f32_to_f16(v[k][2 * i + 1] * sc));
+        *reinterpret_cast<uint4*>(xs + x_pos(static_cast<uint32_t>(gi) * 8u, xl)) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
     if (tid == 0) sm.xexp = e;
   }
 
@@ -249,28 +290,57 @@ struct OprojOp {
     if (lane < 2 * unit_rows()) part[it * 2 * unit_rows() + lane] = rv * ldexpf(1.0f, -sm.xexp);
   }
 
-  __device__ float proj_value(int n, float y) const {
-    if (nvfp4) return round_bf16(round_bf16(y) * __ldg(gsc));
-    return round_bf16(y * bf16_to_f32(row_scale[n]));
-  }
-
-  __device__ void final_epilogue(StreamSmem& sm, uint8_t* xbuf, int tid) const {
-    float* y = reinterpret_cast<float*>(xbuf);
-    for (int n = tid; n < H; n += kConsumerThreads) y[n] = __ldcg(part + n);
+  // Thread tid < H/8 owns outputs [8*tid, 8*tid + 8) and issues all of its loads first.
+  __device__ void final_epilogue(StreamSmem& sm, uint8_t*, int tid) const {
+    const bool mine = tid < H / 8;
+    float y[8];
+    uint4 rv = make_uint4(0u, 0u, 0u, 0u), wv = rv, sv = rv;
+    if (mine) {
+      const float4 p0 = __ldcg(reinterpret_cast<const float4*>(part) + 2 * tid);
+      const float4 p1 = __ldcg(reinterpret_cast<const float4*>(part) + 2 * tid + 1);
+      y[0] = p0.x, y[1] = p0.y, y[2] = p0.z, y[3] = p0.w, y[4] = p1.x, y[5] = p1.y, y[6] = p1.z, y[7] = p1.w;
+      if (ybuf == nullptr) {
+        rv = *reinterpret_cast<const uint4*>(residual + 8 * tid);
+        wv = __ldg(reinterpret_cast<const uint4*>(post_w) + tid);
+        if (!nvfp4) sv = __ldg(reinterpret_cast<const uint4*>(row_scale) + tid);
+      }
+    }
     if (ybuf != nullptr) {
-      for (int n = tid; n < H; n += kConsumerThreads) ybuf[n] = y[n];
+      if (mine) {
+        reinterpret_cast<float4*>(ybuf)[2 * tid] = make_float4(y[0], y[1], y[2], y[3]);
+        reinterpret_cast<float4*>(ybuf)[2 * tid + 1] = make_float4(y[4], y[5], y[6], y[7]);
+      }
       return;
     }
+    const float gs = nvfp4 ? __ldg(gsc) : 0.f;
+    const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
     float ss = 0.f;
-    for (int n = tid; n < H; n += kConsumerThreads) {
-      const float pv = proj_value(n, y[n]);
-      y[n] = pv;
-      ss = __fadd_rn(ss, __fmul_rn(pv, pv));
+    if (mine) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float rsc = bf16_to_f32(static_cast<uint16_t>((i & 1) ? sw[i >> 1] >> 16 : sw[i >> 1] & 0xFFFFu));
+        const float pv = nvfp4 ? round_bf16(round_bf16(y[i]) * gs) : round_bf16(y[i] * rsc);
+        y[i] = pv;
+        ss = __fadd_rn(ss, __fmul_rn(pv, pv));
+      }
     }
     const float r = rms_factor(consumer_sum(ss, sm.scratch), H);
-    for (int n = tid; n < H; n += kConsumerThreads) {
-      const float nb = round_bf16(__fmul_rn(__fmul_rn(y[n], r), bf16_to_f32(post_w[n])));
-      residual[n] = f32_to_bf16(__fadd_rn(bf16_to_f32(residual[n]), nb));
+    if (mine) {
+      const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint16_t h2[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const float res = bf16_to_f32(static_cast<uint16_t>(j ? rw[i] >> 16 : rw[i] & 0xFFFFu));
+          const float pw = bf16_to_f32(static_cast<uint16_t>(j ? ww[i] >> 16 : ww[i] & 0xFFFFu));
+          const float nb = round_bf16(__fmul_rn(__fmul_rn(y[2 * i + j], r), pw));
+          h2[j] = f32_to_bf16(__fadd_rn(res, nb));
+        }
+        o[i] = pack_u16x2(h2[0], h2[1]);
+      }
+      *reinterpret_cast<uint4*>(residual + 8 * tid) = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
 };
@@ -321,7 +391,6 @@ struct LmHeadOp {
     u.scales = nullptr;
     u.code_stride = H * 2;
     u.scale_stride = 0;
-    u.xoff = 0;
     return u;
   }
   __device__ uint32_t* status() const { return &scr->status; }
@@ -329,8 +398,9 @@ struct LmHeadOp {
   __device__ bool has_final() const { return false; }
   __device__ bool between_phases(StreamSmem&, int, uint64_t) const { return true; }
   __device__ void final_epilogue(StreamSmem&, uint8_t*, int) const {}
-  __device__ void stage(StreamSmem& sm, uint8_t* xbuf, int, int tid) const {
-    stage_rmsnorm(x, w_norm, H, reinterpret_cast<uint16_t*>(xbuf), false, sm.scratch);
+  __device__ void prefetch_tail(int, int) const {}
+  __device__ void stage(StreamSmem& sm, uint8_t* xbuf, int, int tid, const XLayout& xl) const {
+    stage_rmsnorm(x, w_norm, H, reinterpret_cast<uint16_t*>(xbuf), false, sm.scratch, xl);
     if (tid == 0) sm.xexp = 0;
   }
   __device__ void item_epilogue(StreamSmem&, int, int it, int lane, float v) const {

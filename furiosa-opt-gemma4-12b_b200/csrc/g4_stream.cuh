@@ -40,7 +40,6 @@ struct UnitDesc {
   const uint8_t* scales;  // NVFP4 block scales of the first row (else unused)
   uint32_t code_stride;   // global bytes between consecutive real rows
   uint32_t scale_stride;
-  uint32_t xoff;          // activation element offset of segment 0
 };
 
 // Geometry shared by every unit of one phase of a launch.
@@ -108,10 +107,68 @@ __host__ __device__ inline StreamLayout make_layout(uint32_t slot_bytes, uint32_
   return l;
 }
 
+// Chunks (64 code bytes of every pseudo-row) one compute warp handles per item, at most.
+constexpr int kMaxChunks = 3;
+
 // Host-side check of a unit geometry against the strides a launch will use.
 __host__ inline bool geom_ok(const UnitGeom& g, uint32_t code_stride, uint32_t scale_stride) {
   const bool contiguous = code_stride == g.q * g.rb && (g.sb == 0 || scale_stride == g.q * g.sb);
-  return g.rb % 64u == 0 && (g.q == 1 || g.q == 2 || g.q == 4) && contiguous && (8u * g.sb) % 16u == 0;
+  return g.rb % 64u == 0 && g.rb / 64u <= static_cast<uint32_t>(kMaxChunks * kComputeWarps) &&
+         (g.q == 1 || g.q == 2 || g.q == 4) && contiguous && (8u * g.sb) % 16u == 0;
+}
+
+// ------------------------------------------------------------------ activation layout
+// The activation vector sits in shared memory permuted so that each lane's B-fragment
+// values of one chunk are 16-byte "pairs" (two MMA steps) it reads with one 16-byte
+// load.  Element k of K lies in segment s = k / seg; inside the segment, chunk c holds
+// kElems elements: lane t owns elements [t*kElems/4, (t+1)*kElems/4) of the chunk, in
+// pairs of 8.  Pair p of lane t is stored at ((p ^ (c & 1)) * 32 + t * 8) elements into
+// the chunk (the XOR only when a lane has 2+ pairs), so the two pseudo-rows one 8-lane
+// shared-memory phase serves -- always one chunk apart -- read different bank halves.
+template <Fmt F>
+struct FmtTraits;
+template <>
+struct FmtTraits<Fmt::NVFP4> {
+  static constexpr uint32_t kElems = 128, kSteps = 8, kPairs = 4;
+};
+template <>
+struct FmtTraits<Fmt::FP8> {
+  static constexpr uint32_t kElems = 64, kSteps = 4, kPairs = 2;
+};
+template <>
+struct FmtTraits<Fmt::BF16> {
+  static constexpr uint32_t kElems = 32, kSteps = 2, kPairs = 1;
+};
+
+struct XLayout {
+  uint32_t seg;       // activation elements per K segment
+  uint32_t log_elems; // log2(elements per chunk)
+  uint32_t swz;       // 1: pair index XOR chunk parity
+};
+
+__host__ __device__ inline XLayout make_xlayout(Fmt f, const UnitGeom& g) {
+  XLayout x;
+  x.seg = g.seg;
+  x.log_elems = (f == Fmt::NVFP4) ? 7u : (f == Fmt::FP8 ? 6u : 5u);
+  x.swz = (f == Fmt::BF16) ? 0u : 1u;
+  return x;
+}
+
+// Shared-memory element index of activation element k (at most 4 segments).
+__device__ __forceinline__ uint32_t x_pos(uint32_t k, const XLayout& xl) {
+  uint32_t s = 0, kk = k;
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    if (kk >= xl.seg) {
+      kk -= xl.seg;
+      ++s;
+    }
+  }
+  const uint32_t c = kk >> xl.log_elems, i = kk & ((1u << xl.log_elems) - 1u);
+  const uint32_t lane_elems_log = xl.log_elems - 2u;
+  const uint32_t t = i >> lane_elems_log, w = i & ((1u << lane_elems_log) - 1u);
+  const uint32_t p = (w >> 3) ^ (xl.swz & c);
+  return s * xl.seg + (c << xl.log_elems) + p * 32u + t * 8u + (w & 7u);
 }
 
 // ------------------------------------------------------------------------ producer
@@ -125,48 +182,90 @@ __device__ __forceinline__ void issue_unit(const UnitDesc& u, const UnitGeom& g,
 }
 
 // ------------------------------------------------------------------------ consumer math
-// Shared-memory operands of one chunk (64 code bytes of every pseudo-row) of an item.
-struct ChunkRegs {
-  uint4 qa, qb;        // this lane's 16 code bytes of its A and B pseudo-rows
-  uint32_t sca, scb;   // NVFP4: the two E4M3 block scales of those bytes, as f16x2
-  uint32_t xaddr;      // shared byte address of this lane's B-fragment activations
-  bool xlane;          // this lane carries a live MMA column
+// Item-invariant shared-memory offsets of one lane for one phase.  Lane (grp, t) loads
+// bytes [ch*64 + t*16, +16) of pseudo-row grp of the A (and B) slot, where the chunk
+// ch = c + rot is this warp's chunk c rotated by the row's MMA column, and feeds MMA
+// column grp with the matching activation fragment.
+//   q >= 2: pseudo-row grp is segment grp % q; column = segment, rotation = segment.
+//   q == 1: one segment; even/odd rows take columns 0/1 and rotations 0/1, so the two
+//           rows of every 8-lane phase are one chunk (64 bytes) apart.
+// B's pseudo-rows use column + 4.  Columns no row uses get an arbitrary (in-bounds)
+// activation fragment: MMA columns are independent, so their sums are never read.
+struct LanePlan {
+  uint32_t roff[kMaxChunks];  // code bytes from the slot base
+  uint32_t soff[kMaxChunks];  // block-scale bytes from the slot base (NVFP4)
+  uint32_t xe[kMaxChunks];    // activation bytes of even pairs from the x buffer
+  uint32_t xo[kMaxChunks];    // ... of odd pairs
+  int nc;                     // chunks of this warp
+  int col;                    // MMA column of this lane's A pseudo-row (B: col + 4)
 };
 
-// Where lane (grp, t) reads chunk c:  its A/B pseudo-rows are row grp of each slot,
-// at column s = grp % q; column j of the MMA carries segment j (A) or j-4 (B); each
-// column walks the chunks rotated by its segment.
 template <Fmt F>
-__device__ __forceinline__ ChunkRegs load_chunk(uint32_t sa, uint32_t sbs, bool has_b, const UnitGeom& g, int c,
-                                                int lane, uint32_t xa, uint32_t xb, int nch) {
-  ChunkRegs r;
+__device__ __forceinline__ LanePlan make_plan(const UnitGeom& g, int warp, int lane, bool has_b) {
+  using T = FmtTraits<F>;
+  LanePlan pl;
   const int grp = lane >> 2, t = lane & 3;
-  const int q = static_cast<int>(g.q);
-  const int ch = (c + grp % q) % nch;
-  const uint32_t roff = grp * g.rb + ch * 64 + t * 16;
+  const int q = static_cast<int>(g.q), nch = static_cast<int>(g.rb / 64u);
+  const int rot = (q == 1) ? (grp & 1) : (grp & (q - 1));
+  pl.col = rot;
+  // the activation this lane supplies: column grp (A) or grp - 4 (B)
+  const int cg = grp & 3;
+  bool live = cg < ((q == 1) ? 2 : q);
+  if (grp >= 4 && !has_b) live = false;
+  const int xs = (live && q > 1) ? cg : 0;
+  const int xr = live ? cg : 0;
+  int n = 0;
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int c = warp + i * kComputeWarps;
+    pl.roff[i] = pl.soff[i] = pl.xe[i] = pl.xo[i] = 0u;
+    if (c < nch) {
+      int ch = c + rot;
+      if (ch >= nch) ch -= nch;
+      int xc = c + xr;
+      if (xc >= nch) xc -= nch;
+      pl.roff[i] = static_cast<uint32_t>(grp) * g.rb + static_cast<uint32_t>(ch) * 64u + static_cast<uint32_t>(t) * 16u;
+      pl.soff[i] = 8u * g.rb + static_cast<uint32_t>(grp) * g.sb + static_cast<uint32_t>(ch) * 8u + static_cast<uint32_t>(t) * 2u;
+      const uint32_t sw = (T::kPairs > 1) ? static_cast<uint32_t>(xc & 1) : 0u;
+      const uint32_t base = 2u * (static_cast<uint32_t>(xs) * g.seg + static_cast<uint32_t>(xc) * T::kElems +
+                                  static_cast<uint32_t>(t) * 8u);
+      pl.xe[i] = base + sw * 64u;
+      pl.xo[i] = base + (sw ^ 1u) * 64u;
+      ++n;
+    }
+  }
+  pl.nc = n;
+  return pl;
+}
+
+// Code and scale registers of one chunk.
+struct ChunkRegs {
+  uint4 qa, qb;       // this lane's 16 code bytes of its A and B pseudo-rows
+  uint32_t sca, scb;  // NVFP4: their two E4M3 block scales, as f16x2
+};
+
+template <Fmt F, bool kHasB>
+__device__ __forceinline__ ChunkRegs load_chunk(uint32_t sa, uint32_t sb, uint32_t roff, uint32_t soff) {
+  ChunkRegs r;
   r.qa = lds128(sa + roff);
-  r.qb = has_b ? lds128(sbs + roff) : make_uint4(0, 0, 0, 0);
+  r.qb = kHasB ? lds128(sb + roff) : make_uint4(0u, 0u, 0u, 0u);
   if constexpr (F == Fmt::NVFP4) {
-    const uint32_t soff = 8u * g.rb + grp * g.sb + ch * 8 + t * 2;
     r.sca = cvt_e4m3x2(lds16(sa + soff));
-    r.scb = has_b ? cvt_e4m3x2(lds16(sbs + soff)) : 0u;
+    r.scb = kHasB ? cvt_e4m3x2(lds16(sb + soff)) : 0u;
   } else {
     r.sca = r.scb = 0u;
   }
-  const int xs = (grp < 4) ? grp : grp - 4;
-  r.xlane = (grp < q) || (grp >= 4 && xs < q && has_b);
-  const uint32_t xbase = (grp < 4 ? xa : xb) + xs * g.seg * 2;
-  const int xch = (c + xs) % nch;
-  constexpr int kElems = (F == Fmt::NVFP4) ? 128 : (F == Fmt::FP8 ? 64 : 32);  // per chunk
-  r.xaddr = xbase + (xch * kElems + t * (kElems / 4)) * 2;
   return r;
 }
 
 // Contract one chunk: MMA step j accumulates into acc[j & 1] (two independent chains).
+// Step j uses this lane's elements 4j..4j+3 of the chunk: A from the decoded code
+// registers, B = activation pair j/2 (one 16-byte load feeds steps 2p and 2p+1).
 template <Fmt F, bool kHasB>
-__device__ __forceinline__ void compute_chunk(float (&acc0)[4], float (&acc1)[4], const ChunkRegs& r) {
+__device__ __forceinline__ void compute_chunk(float (&acc0)[4], float (&acc1)[4], const ChunkRegs& r, uint32_t xe,
+                                              uint32_t xo) {
+  using T = FmtTraits<F>;
   if constexpr (F == Fmt::NVFP4) {
-    // lane t holds physical k [128ch+32t, +32): byte i -> k 128ch+32t+2i+{0,1}
     uint32_t fa[16], fb[16];
     cvt_e2m1x8(r.qa.x, fa[0], fa[1], fa[2], fa[3]);
     cvt_e2m1x8(r.qa.y, fa[4], fa[5], fa[6], fa[7]);
@@ -179,79 +278,68 @@ __device__ __forceinline__ void compute_chunk(float (&acc0)[4], float (&acc1)[4]
       cvt_e2m1x8(r.qb.w, fb[12], fb[13], fb[14], fb[15]);
     }
     const uint32_t sal = dup_lo(r.sca), sah = dup_hi(r.sca);
-    const uint32_t sbl = dup_lo(r.scb), sbh = dup_hi(r.scb);
+    const uint32_t sbl = kHasB ? dup_lo(r.scb) : 0u, sbh = kHasB ? dup_hi(r.scb) : 0u;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint32_t s_a = (j < 4) ? sal : sah;
-      const uint32_t a0 = hmul2_u32(fa[2 * j], s_a);
-      const uint32_t a2 = hmul2_u32(fa[2 * j + 1], s_a);
-      uint32_t a1 = 0u, a3 = 0u;
-      if constexpr (kHasB) {
-        const uint32_t s_b = (j < 4) ? sbl : sbh;
-        a1 = hmul2_u32(fb[2 * j], s_b);
-        a3 = hmul2_u32(fb[2 * j + 1], s_b);
+    for (int p = 0; p < static_cast<int>(T::kPairs); ++p) {
+      const uint4 x = lds128(((p & 1) ? xo : xe) + static_cast<uint32_t>(p >> 1) * 128u);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int j = 2 * p + h;
+        const uint32_t s_a = (j < 4) ? sal : sah;
+        const uint32_t a0 = hmul2_u32(fa[2 * j], s_a);
+        const uint32_t a2 = hmul2_u32(fa[2 * j + 1], s_a);
+        uint32_t a1 = 0u, a3 = 0u;
+        if constexpr (kHasB) {
+          const uint32_t s_b = (j < 4) ? sbl : sbh;
+          a1 = hmul2_u32(fb[2 * j], s_b);
+          a3 = hmul2_u32(fb[2 * j + 1], s_b);
+        }
+        if (h)
+          mma_f16(acc1, a0, a1, a2, a3, x.z, x.w);
+        else
+          mma_f16(acc0, a0, a1, a2, a3, x.x, x.y);
       }
-      uint2 b = make_uint2(0, 0);
-      if (r.xlane) b = lds64(r.xaddr + 8 * j);
-      if (j & 1)
-        mma_f16(acc1, a0, a1, a2, a3, b.x, b.y);
-      else
-        mma_f16(acc0, a0, a1, a2, a3, b.x, b.y);
     }
   } else if constexpr (F == Fmt::FP8) {
-    // lane t holds physical k [64ch+16t, +16): bytes 4j..4j+3 -> k 64ch+16t+4j+{0..3}
     const uint32_t wa[4] = {r.qa.x, r.qa.y, r.qa.z, r.qa.w};
     const uint32_t wb[4] = {r.qb.x, r.qb.y, r.qb.z, r.qb.w};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t a0 = cvt_e4m3x2(static_cast<uint16_t>(wa[j] & 0xFFFFu));
-      const uint32_t a2 = cvt_e4m3x2(static_cast<uint16_t>(wa[j] >> 16));
-      uint32_t a1 = 0u, a3 = 0u;
-      if constexpr (kHasB) {
-        a1 = cvt_e4m3x2(static_cast<uint16_t>(wb[j] & 0xFFFFu));
-        a3 = cvt_e4m3x2(static_cast<uint16_t>(wb[j] >> 16));
+    for (int p = 0; p < static_cast<int>(T::kPairs); ++p) {
+      const uint4 x = lds128(((p & 1) ? xo : xe) + static_cast<uint32_t>(p >> 1) * 128u);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int j = 2 * p + h;
+        const uint32_t a0 = cvt_e4m3x2(static_cast<uint16_t>(wa[j] & 0xFFFFu));
+        const uint32_t a2 = cvt_e4m3x2(static_cast<uint16_t>(wa[j] >> 16));
+        uint32_t a1 = 0u, a3 = 0u;
+        if constexpr (kHasB) {
+          a1 = cvt_e4m3x2(static_cast<uint16_t>(wb[j] & 0xFFFFu));
+          a3 = cvt_e4m3x2(static_cast<uint16_t>(wb[j] >> 16));
+        }
+        if (h)
+          mma_f16(acc1, a0, a1, a2, a3, x.z, x.w);
+        else
+          mma_f16(acc0, a0, a1, a2, a3, x.x, x.y);
       }
-      uint2 b = make_uint2(0, 0);
-      if (r.xlane) b = lds64(r.xaddr + 8 * j);
-      if (j & 1)
-        mma_f16(acc1, a0, a1, a2, a3, b.x, b.y);
-      else
-        mma_f16(acc0, a0, a1, a2, a3, b.x, b.y);
     }
   } else {
-    // bf16: lane t holds physical k [32ch+8t, +8): word i -> k 32ch+8t+2i+{0,1}
-    const uint32_t wa[4] = {r.qa.x, r.qa.y, r.qa.z, r.qa.w};
-    const uint32_t wb[4] = {r.qb.x, r.qb.y, r.qb.z, r.qb.w};
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      uint2 b = make_uint2(0, 0);
-      if (r.xlane) b = lds64(r.xaddr + 8 * j);
-      if (j & 1)
-        mma_bf16(acc1, wa[2 * j], wb[2 * j], wa[2 * j + 1], wb[2 * j + 1], b.x, b.y);
-      else
-        mma_bf16(acc0, wa[2 * j], wb[2 * j], wa[2 * j + 1], wb[2 * j + 1], b.x, b.y);
-    }
+    const uint4 x = lds128(xe);
+    mma_bf16(acc0, r.qa.x, r.qb.x, r.qa.y, r.qb.y, x.x, x.y);
+    mma_bf16(acc1, r.qa.z, r.qb.z, r.qa.w, r.qb.w, x.z, x.w);
   }
 }
 
-// This warp's share of an item: chunks warp, warp+NW, ... with the next chunk's shared
-// loads issued before the current chunk's math.
+// This warp's share of an item: its pl.nc chunks, each chunk's codes loaded right before
+// its math (a one-chunk look-ahead costs more registers than it hides latency).
 template <Fmt F, bool kHasB>
-__device__ __forceinline__ void item_mma(float (&acc)[4], uint32_t sa, uint32_t sbs, const UnitGeom& g, int warp,
-                                         int lane, uint32_t xa, uint32_t xb) {
-  const int nch = static_cast<int>(g.rb / 64u);
+__device__ __forceinline__ void item_mma(float (&acc)[4], uint32_t sa, uint32_t sb, uint32_t xbase,
+                                         const LanePlan& pl) {
   float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
-  int c = warp;
-  if (c < nch) {
-    ChunkRegs cur = load_chunk<F>(sa, sbs, kHasB, g, c, lane, xa, xb, nch);
-    while (true) {
-      const int cn = c + kComputeWarps;
-      ChunkRegs nxt;
-      if (cn < nch) nxt = load_chunk<F>(sa, sbs, kHasB, g, cn, lane, xa, xb, nch);
-      compute_chunk<F, kHasB>(acc0, acc1, cur);
-      if (cn >= nch) break;
-      cur = nxt;
-      c = cn;
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    if (i < pl.nc) {
+      const ChunkRegs cur = load_chunk<F, kHasB>(sa, sb, pl.roff[i], pl.soff[i]);
+      compute_chunk<F, kHasB>(acc0, acc1, cur, xbase + pl.xe[i], xbase + pl.xo[i]);
     }
   }
 #pragma unroll
@@ -261,13 +349,15 @@ __device__ __forceinline__ void item_mma(float (&acc)[4], uint32_t sa, uint32_t 
 // ------------------------------------------------------------------------ kernel body
 // Op interface (all __device__ const members):
 //   static constexpr Fmt kFmt; static constexpr int kPhases;
-//   int items(int phase); UnitGeom geom(int phase); UnitDesc unit(int phase, int item, int half);
-//   void stage(StreamSmem&, uint8_t* xbuf, int phase, int tid)      [consumer threads]
+//   int items(int phase); UnitGeom geom(int phase); UnitDesc unit(int phase, int item, int half)
+//       (unit B of every item of a phase is present, or absent for every item);
+//   void stage(StreamSmem&, uint8_t* xbuf, int phase, int tid, const XLayout&)  [consumers]
 //   void item_epilogue(StreamSmem&, int phase, int item, int lane, float v)  [one warp]
 //       lanes 0-7: pseudo-rows of unit A, lanes 8-15: pseudo-rows of unit B
 //   bool has_final(); void final_epilogue(StreamSmem&, uint8_t* xbuf, int tid) [last CTA]
 //   uint32_t* done_counter(); uint32_t* status();
 //   bool between_phases(StreamSmem&, int phase, uint64_t deadline)  [consumer threads]
+//   void prefetch_tail(int cta, int lane)   [epilogue warp, at start: L2 prefetches]
 template <class Op>
 __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& lay, uint32_t slot_bytes,
                                             uint64_t budget_ns) {
@@ -298,104 +388,114 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------------------ producer
     // kProducerLanes lanes issue in parallel (one thread issues a bulk copy only every
-    // few hundred ns): lane j owns the units k with k % kProducerLanes == j, i.e. slots
-    // j, j + kProducerLanes, ...  Every lane walks the same unit sequence.
+    // few hundred ns).  Every lane walks the same unit sequence k = 0, 1, ...; lane j
+    // issues the units with k % kProducerLanes == j into slots j, j + kProducerLanes,
+    // ... (S is a multiple of kProducerLanes), counting its own refills.
     if (lane < kProducerLanes) {
       const uint64_t pol = l2_evict_first_policy();
-      uint32_t k = 0;
+      uint32_t k = 0, s = static_cast<uint32_t>(lane), use = 0, mine = 0;
       bool ok = true;
       for (int ph = 0; ph < Op::kPhases && ok; ++ph) {
         const int n = op.items(ph);
         const UnitGeom g = op.geom(ph);
+        const int halves = (op.unit(ph, 0, 1).codes != nullptr) ? 2 : 1;
         for (int it = cta; it < n && ok; it += G) {
 #pragma unroll 1
-          for (int half = 0; half < 2; ++half) {
-            const UnitDesc u = op.unit(ph, it, half);
-            if (u.codes == nullptr) continue;
-            if (k % kProducerLanes == static_cast<uint32_t>(lane)) {
-              const uint32_t s = k % S, use = k / S;
-              if (use > 0 && !mbar_wait_suspend(&sm.empty[s], (use - 1) & 1u, deadline)) {
-                ok = false;
-                break;
-              }
-              issue_unit(u, g, slots + s * slot_bytes, &sm.full[s], pol);
+          for (int half = 0; half < halves; ++half, ++k) {
+            if ((k & (kProducerLanes - 1)) != static_cast<uint32_t>(lane)) continue;
+            if (use > 0 && !mbar_wait_suspend(&sm.empty[s], (use - 1) & 1u, deadline)) {
+              ok = false;
+              break;
             }
-            ++k;
+            issue_unit(op.unit(ph, it, half), g, slots + s * slot_bytes, &sm.full[s], pol);
+            ++mine;
+            s += kProducerLanes;
+            if (s >= S) {
+              s -= S;
+              ++use;
+            }
           }
         }
       }
       if (!ok) atomicOr(op.status(), DEV_ERR_TIMEOUT_MBAR);
-      // drain: no bulk copy may still target this CTA's shared memory when it exits
-      const uint32_t first = (k > S) ? k - S : 0u;
-      for (uint32_t q = first; q < k; ++q)
-        if (q % kProducerLanes == static_cast<uint32_t>(lane))
-          mbar_wait_suspend(&sm.full[q % S], (q / S) & 1u, deadline + budget_ns);
+      // drain: no bulk copy may still target this CTA's shared memory when it exits.
+      // This lane's r-th slot (lane + r*kProducerLanes) took fills r, r + S/lanes, ...
+      const uint32_t per = S / kProducerLanes;
+      for (uint32_t r = 0; r < per; ++r) {
+        if (mine <= r) break;
+        const uint32_t fills = (mine - r - 1) / per + 1;
+        mbar_wait_suspend(&sm.full[lane + r * kProducerLanes], (fills - 1) & 1u, deadline + budget_ns);
+      }
     }
     return;
   }
 
   // -------------------------------------------------------------------- consumers
-  uint32_t k = 0, items_done = 0;
+  // The epilogue warp is idle until the first item completes: it pulls the operands of
+  // the op's final epilogue into L2 now, so the last CTA's tail finds them there.
+  if (warp == kEpilogueWarp) op.prefetch_tail(cta, lane);
+  uint32_t slot = 0, spar = 0;                 // next slot to consume, its fill parity
+  uint32_t rbuf = 0, rpar = 0, items_done = 0; // reduction buffer ring
   bool ok = true;
+  const int grp = lane >> 2, t = lane & 3;
+  const uint32_t xbase = smem_u32(xbuf), slot0 = smem_u32(slots);
   for (int ph = 0; ph < Op::kPhases; ++ph) {
     if (ph > 0) {
       if (!op.between_phases(sm, ph, deadline)) ok = false;
     }
-    op.stage(sm, xbuf, ph, tid);
+    const UnitGeom g = op.geom(ph);
+    op.stage(sm, xbuf, ph, tid, make_xlayout(Op::kFmt, g));
     named_bar_sync(kBarConsumers, kConsumerThreads);
     if (sm.failed) ok = false;
     const int n = op.items(ph);
-    const UnitGeom g = op.geom(ph);
-    const int grp = lane >> 2, t = lane & 3;
-    const int sq = grp % static_cast<int>(g.q);
+    const bool has_b = op.unit(ph, 0, 1).codes != nullptr;
+    const LanePlan pl = make_plan<Op::kFmt>(g, warp, lane, has_b);
     for (int it = cta; it < n; it += G) {
-      const UnitDesc ua = op.unit(ph, it, 0);
-      const UnitDesc ub = op.unit(ph, it, 1);
-      const bool has_b = ub.codes != nullptr;
-      const uint32_t sa_i = k % S, ua_use = k / S;
-      ++k;
-      uint32_t sb_i = 0, ub_use = 0;
+      const uint32_t sa_i = slot, pa = spar;
+      if (++slot == S) {
+        slot = 0;
+        spar ^= 1u;
+      }
+      uint32_t sb_i = sa_i, pb = pa;
       if (has_b) {
-        sb_i = k % S;
-        ub_use = k / S;
-        ++k;
+        sb_i = slot;
+        pb = spar;
+        if (++slot == S) {
+          slot = 0;
+          spar ^= 1u;
+        }
       }
       // Reduction buffer ring: item i uses buffer i % S.  Compute warps write their
       // partial sums and arrive on redbar (release); the epilogue warp waits on it
       // (acquire), sums, marks the buffer free on redfree and runs the item's epilogue.
       // Compute warps release a slot as soon as their own math is done, never wait for
       // one another, and only wait for a buffer to be free before reusing it S items on.
-      const int rbuf = static_cast<int>(items_done % S);
-      const uint32_t rpar = (items_done / S) & 1u;
       if (warp != kEpilogueWarp) {
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         if (ok) {
-          ok = mbar_wait(&sm.full[sa_i], ua_use & 1u, deadline);
-          if (ok && has_b) ok = mbar_wait(&sm.full[sb_i], ub_use & 1u, deadline);
+          ok = mbar_wait_suspend(&sm.full[sa_i], pa, deadline);
+          if (ok && has_b) ok = mbar_wait_suspend(&sm.full[sb_i], pb, deadline);
         }
         if (ok) {
-          const uint32_t sa = smem_u32(slots + sa_i * slot_bytes);
-          const uint32_t sbb = has_b ? smem_u32(slots + sb_i * slot_bytes) : sa;
-          const uint32_t xa = smem_u32(xbuf) + 2u * ua.xoff;
-          const uint32_t xb = smem_u32(xbuf) + 2u * (has_b ? ub.xoff : ua.xoff);
+          const uint32_t sa = slot0 + sa_i * slot_bytes, sb = slot0 + sb_i * slot_bytes;
           if (has_b)
-            item_mma<Op::kFmt, true>(acc, sa, sbb, g, warp, lane, xa, xb);
+            item_mma<Op::kFmt, true>(acc, sa, sb, xbase, pl);
           else
-            item_mma<Op::kFmt, false>(acc, sa, sbb, g, warp, lane, xa, xb);
+            item_mma<Op::kFmt, false>(acc, sa, sb, xbase, pl);
         }
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&sm.empty[sa_i]);
           if (has_b) mbar_arrive(&sm.empty[sb_i]);
         }
-        if (items_done >= S && ok && !mbar_wait(&sm.redfree[rbuf], rpar ^ 1u, deadline)) ok = false;
-        // pseudo-row grp of A sits at (row grp, column sq), of B at (row grp+8, column 4+sq)
-        if (t == (sq >> 1)) sm.red[rbuf][warp][grp] = (sq & 1) ? acc[1] : acc[0];
-        if (t == 2 + (sq >> 1)) sm.red[rbuf][warp][8 + grp] = (sq & 1) ? acc[3] : acc[2];
+        if (items_done >= S && ok && !mbar_wait_suspend(&sm.redfree[rbuf], rpar ^ 1u, deadline)) ok = false;
+        // pseudo-row grp of A sits at (row grp, column col), of B at (row grp+8, column 4+col)
+        if (t == (pl.col >> 1)) sm.red[rbuf][warp][grp] = (pl.col & 1) ? acc[1] : acc[0];
+        if (t == 2 + (pl.col >> 1)) sm.red[rbuf][warp][8 + grp] = (pl.col & 1) ? acc[3] : acc[2];
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.redbar[rbuf]);
       } else {
-        if (ok && !mbar_wait(&sm.redbar[rbuf], rpar, deadline, true)) ok = false;
+        if (ok && !mbar_wait_suspend(&sm.redbar[rbuf], rpar, deadline)) ok = false;
         float v = 0.f;
         if (lane < 16) {
 #pragma unroll
@@ -406,6 +506,10 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
         if (ok) op.item_epilogue(sm, ph, it, lane, v);
       }
       ++items_done;
+      if (++rbuf == S) {
+        rbuf = 0;
+        rpar ^= 1u;
+      }
     }
     if (!ok && tid == 0) atomicOr(op.status(), DEV_ERR_TIMEOUT_MBAR);
   }
@@ -413,19 +517,15 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
   if (op.has_final()) {
     named_bar_sync(kBarConsumers, kConsumerThreads);
     if (tid == 0) {
-      __threadfence();
+      // acq_rel: releases this CTA's partial sums, and in the last CTA acquires everyone's
       const uint32_t old = atom_add_acq_rel_gpu(op.done_counter(), 1u);
       sm.is_last = (old == static_cast<uint32_t>(G - 1)) ? 1 : 0;
     }
     named_bar_sync(kBarConsumers, kConsumerThreads);
     if (sm.is_last) {
-      __threadfence();
       op.final_epilogue(sm, xbuf, tid);
       named_bar_sync(kBarConsumers, kConsumerThreads);
-      if (tid == 0) {
-        *op.done_counter() = 0u;
-        __threadfence();
-      }
+      if (tid == 0) *op.done_counter() = 0u;  // visible to the next launch at kernel end
     }
   }
 }
@@ -453,8 +553,7 @@ __device__ __forceinline__ bool grid_wait(uint32_t* counter, uint32_t target, ui
                                           uint32_t* status, StreamSmem& sm) {
   named_bar_sync(kBarConsumers, kConsumerThreads);
   if (threadIdx.x == 0) {
-    __threadfence();
-    atom_add_release_gpu(counter, 1u);
+    red_add_release_gpu(counter, 1u);  // release covers this CTA's writes (ordered by the bar.sync)
     uint32_t spins = 0;
     int fail = 0;
     while (ld_acquire_gpu(counter) < target) {
@@ -497,7 +596,7 @@ __device__ __forceinline__ float consumer_max(float v, float* scratch) {
 // RMSNorm of a bf16 vector (global) into shared memory as scaled f16 (or bf16) MMA
 // operands, by the consumer threads.  Returns the scale exponent (0 for bf16 output).
 __device__ __forceinline__ int stage_rmsnorm(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
-                                             int n, uint16_t* xs, bool as_f16, float* scratch) {
+                                             int n, uint16_t* xs, bool as_f16, float* scratch, const XLayout& xl) {
   // 8 elements (16 bytes) per thread and step; n % 8 == 0, pointers 16-byte aligned
   const int tid = threadIdx.x;
   constexpr int kMaxGroups = 2;  // n <= 2 * 8 * kConsumerThreads
@@ -552,7 +651,7 @@ __device__ __forceinline__ int stage_rmsnorm(const uint16_t* __restrict__ x, con
       for (int i = 0; i < 4; ++i)
         o[i] = as_f16 ? pack_u16x2(f32_to_f16(y[k][2 * i] * sc), f32_to_f16(y[k][2 * i + 1] * sc))
                       : pack_u16x2(f32_to_bf16(y[k][2 * i]), f32_to_bf16(y[k][2 * i + 1]));
-      reinterpret_cast<uint4*>(xs)[gi] = make_uint4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<uint4*>(xs + x_pos(static_cast<uint32_t>(gi) * 8u, xl)) = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
   named_bar_sync(kBarConsumers, kConsumerThreads);
