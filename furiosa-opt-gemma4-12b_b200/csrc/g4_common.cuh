@@ -172,6 +172,20 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
+// Arrive only where `pred` holds, as a predicated instruction (no divergent branch).
+__device__ __forceinline__ void mbar_arrive_if(uint64_t* bar, bool pred) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+      "@p mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];\n\t}" ::"r"(smem_u32(bar)),
+      "r"(static_cast<uint32_t>(pred))
+      : "memory");
+}
+// Shared-memory f32 store only where `pred` holds, as a predicated instruction.
+__device__ __forceinline__ void sts_f32_if(uint32_t addr, float v, bool pred) {
+  asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t@p st.shared.f32 [%0], %1;\n\t}" ::"r"(addr),
+               "f"(v), "r"(static_cast<uint32_t>(pred))
+               : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(
                    smem_u32(bar)),

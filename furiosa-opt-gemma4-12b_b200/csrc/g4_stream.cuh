@@ -70,19 +70,20 @@ __host__ __device__ inline UnitGeom make_geom(Fmt f, uint32_t rb, uint32_t q) {
 constexpr int kComputeWarps = G4_COMPUTE_WARPS;
 constexpr int kEpilogueWarp = kComputeWarps;
 constexpr int kConsumerWarps = kComputeWarps + 1;
-constexpr int kMaxSlots = 8;
-constexpr int kProducerLanes = 4;  // slot counts are multiples of this
+constexpr int kMaxSlots = 8;       // unit slots of a launch's layout (two per item slot)
+constexpr int kRedSlots = 8;       // reduction buffers (ring over items)
+constexpr int kProducerLanes = 4;  // issuing lanes; item slots = a multiple of this
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr uint32_t kBarConsumers = 1;  // named barrier id among consumer warps
 
 // Shared-memory header of a streaming kernel (the x buffer and the slots follow).
 struct StreamSmem {
-  uint64_t full[16];
-  uint64_t empty[16];
-  uint64_t redbar[kMaxSlots];                 // all compute warps wrote the buffer's partials
-  uint64_t redfree[kMaxSlots];                // the epilogue warp has read the buffer
-  float red[kMaxSlots][kComputeWarps][16];   // per-item partial sums, ring of S buffers
+  uint64_t full[kMaxSlots / 2];               // item slot filled (both units landed)
+  uint64_t empty[kMaxSlots / 2];              // every compute warp is done with the item slot
+  uint64_t redbar[kRedSlots];                 // all compute warps wrote the buffer's partials
+  uint64_t redfree[kRedSlots];                // the epilogue warp has read the buffer
+  float red[kRedSlots][kComputeWarps][16];    // per-item partial sums, ring of buffers
   float scratch[64];        // op-defined (norm reductions, flags)
   int xexp;                 // activation scale exponent: x16 = x * 2^xexp
   int is_last;              // this CTA completed the launch (runs the final epilogue)
@@ -172,13 +173,17 @@ __device__ __forceinline__ uint32_t x_pos(uint32_t k, const XLayout& xl) {
 }
 
 // ------------------------------------------------------------------------ producer
-// One copy for the unit's 8 pseudo-rows of codes, one for their block scales.
-__device__ __forceinline__ void issue_unit(const UnitDesc& u, const UnitGeom& g, uint8_t* slot,
-                                           uint64_t* full, uint64_t policy) {
+// One item into one item slot: unit A at the slot start, unit B one unit stride later;
+// per unit one copy for its 8 pseudo-rows of codes and one for their block scales, all
+// completing on the slot's single "full" barrier.
+__device__ __forceinline__ void issue_item(const UnitDesc& a, const UnitDesc& b, const UnitGeom& g, uint8_t* slot,
+                                           uint32_t unit_stride, uint64_t* full, uint64_t policy) {
   const uint32_t cbytes = 8u * g.rb, sbytes = 8u * g.sb;
-  mbar_arrive_expect_tx(full, cbytes + sbytes);
-  bulk_g2s(slot, u.codes, cbytes, full, policy);
-  if (sbytes) bulk_g2s(slot + cbytes, u.scales, sbytes, full, policy);
+  mbar_arrive_expect_tx(full, 2u * (cbytes + sbytes));
+  bulk_g2s(slot, a.codes, cbytes, full, policy);
+  if (sbytes) bulk_g2s(slot + cbytes, a.scales, sbytes, full, policy);
+  bulk_g2s(slot + unit_stride, b.codes, cbytes, full, policy);
+  if (sbytes) bulk_g2s(slot + unit_stride + cbytes, b.scales, sbytes, full, policy);
 }
 
 // ------------------------------------------------------------------------ consumer math
@@ -350,7 +355,7 @@ __device__ __forceinline__ void item_mma(float (&acc)[4], uint32_t sa, uint32_t 
 // Op interface (all __device__ const members):
 //   static constexpr Fmt kFmt; static constexpr int kPhases;
 //   int items(int phase); UnitGeom geom(int phase); UnitDesc unit(int phase, int item, int half)
-//       (unit B of every item of a phase is present, or absent for every item);
+//       (every item is two units, A = half 0 and B = half 1);
 //   void stage(StreamSmem&, uint8_t* xbuf, int phase, int tid, const XLayout&)  [consumers]
 //   void item_epilogue(StreamSmem&, int phase, int item, int lane, float v)  [one warp]
 //       lanes 0-7: pseudo-rows of unit A, lanes 8-15: pseudo-rows of unit B
@@ -358,8 +363,10 @@ __device__ __forceinline__ void item_mma(float (&acc)[4], uint32_t sa, uint32_t 
 //   uint32_t* done_counter(); uint32_t* status();
 //   bool between_phases(StreamSmem&, int phase, uint64_t deadline)  [consumer threads]
 //   void prefetch_tail(int cta, int lane)   [epilogue warp, at start: L2 prefetches]
+// `unit_bytes` is the launch's unit slot size (>= every phase's 8 * (rb + sb), a multiple
+// of 128); lay.nslots unit slots form lay.nslots / 2 item slots.
 template <class Op>
-__device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& lay, uint32_t slot_bytes,
+__device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& lay, uint32_t unit_bytes,
                                             uint64_t budget_ns) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   StreamSmem& sm = *reinterpret_cast<StreamSmem*>(smem_raw);
@@ -367,7 +374,8 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
   uint8_t* slots = smem_raw + lay.slot_off;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x, cta = blockIdx.x;
-  const uint32_t S = lay.nslots;
+  const uint32_t S = lay.nslots / 2;           // item slots (a multiple of kProducerLanes)
+  const uint32_t item_bytes = 2u * unit_bytes;
   const uint64_t deadline = global_ns() + budget_ns;
 
   if (tid == 0) {
@@ -375,7 +383,7 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], kComputeWarps);
     }
-    for (int s = 0; s < kMaxSlots; ++s) {
+    for (int s = 0; s < kRedSlots; ++s) {
       mbar_init(&sm.redbar[s], kComputeWarps);
       mbar_init(&sm.redfree[s], 1);
     }
@@ -387,10 +395,9 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
 
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------------------ producer
-    // kProducerLanes lanes issue in parallel (one thread issues a bulk copy only every
-    // few hundred ns).  Every lane walks the same unit sequence k = 0, 1, ...; lane j
-    // issues the units with k % kProducerLanes == j into slots j, j + kProducerLanes,
-    // ... (S is a multiple of kProducerLanes), counting its own refills.
+    // kProducerLanes lanes issue in parallel.  Every lane walks the same item sequence
+    // k = 0, 1, ...; lane j issues the items k with k % kProducerLanes == j, into item
+    // slots j, j + kProducerLanes, ... (k % S), counting its own refills of them.
     if (lane < kProducerLanes) {
       const uint64_t pol = l2_evict_first_policy();
       uint32_t k = 0, s = static_cast<uint32_t>(lane), use = 0, mine = 0;
@@ -398,22 +405,18 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
       for (int ph = 0; ph < Op::kPhases && ok; ++ph) {
         const int n = op.items(ph);
         const UnitGeom g = op.geom(ph);
-        const int halves = (op.unit(ph, 0, 1).codes != nullptr) ? 2 : 1;
-        for (int it = cta; it < n && ok; it += G) {
-#pragma unroll 1
-          for (int half = 0; half < halves; ++half, ++k) {
-            if ((k & (kProducerLanes - 1)) != static_cast<uint32_t>(lane)) continue;
-            if (use > 0 && !mbar_wait_suspend(&sm.empty[s], (use - 1) & 1u, deadline)) {
-              ok = false;
-              break;
-            }
-            issue_unit(op.unit(ph, it, half), g, slots + s * slot_bytes, &sm.full[s], pol);
-            ++mine;
-            s += kProducerLanes;
-            if (s >= S) {
-              s -= S;
-              ++use;
-            }
+        for (int it = cta; it < n; it += G, ++k) {
+          if ((k & (kProducerLanes - 1)) != static_cast<uint32_t>(lane)) continue;
+          if (use > 0 && !mbar_wait_suspend(&sm.empty[s], (use - 1) & 1u, deadline)) {
+            ok = false;
+            break;
+          }
+          issue_item(op.unit(ph, it, 0), op.unit(ph, it, 1), g, slots + s * item_bytes, unit_bytes, &sm.full[s], pol);
+          ++mine;
+          s += kProducerLanes;
+          if (s >= S) {
+            s -= S;
+            ++use;
           }
         }
       }
@@ -434,11 +437,14 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
   // The epilogue warp is idle until the first item completes: it pulls the operands of
   // the op's final epilogue into L2 now, so the last CTA's tail finds them there.
   if (warp == kEpilogueWarp) op.prefetch_tail(cta, lane);
-  uint32_t slot = 0, spar = 0;                 // next slot to consume, its fill parity
+  uint32_t slot = 0, spar = 0;                 // next item slot to consume, its fill parity
   uint32_t rbuf = 0, rpar = 0, items_done = 0; // reduction buffer ring
   bool ok = true;
   const int grp = lane >> 2, t = lane & 3;
   const uint32_t xbase = smem_u32(xbuf), slot0 = smem_u32(slots);
+  // this lane's slot in every reduction buffer (compute warps)
+  const uint32_t red0 = smem_u32(&sm.red[0][warp < kComputeWarps ? warp : 0][grp]);
+  constexpr uint32_t kRedStride = sizeof(float) * kComputeWarps * 16;
   for (int ph = 0; ph < Op::kPhases; ++ph) {
     if (ph > 0) {
       if (!op.between_phases(sm, ph, deadline)) ok = false;
@@ -448,52 +454,32 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
     named_bar_sync(kBarConsumers, kConsumerThreads);
     if (sm.failed) ok = false;
     const int n = op.items(ph);
-    const bool has_b = op.unit(ph, 0, 1).codes != nullptr;
-    const LanePlan pl = make_plan<Op::kFmt>(g, warp, lane, has_b);
+    const LanePlan pl = make_plan<Op::kFmt>(g, warp, lane, true);
+    // pseudo-row grp of A sits at (row grp, column col), of B at (row grp+8, column 4+col)
+    const bool st_a = t == (pl.col >> 1), st_b = t == 2 + (pl.col >> 1), odd = (pl.col & 1) != 0;
     for (int it = cta; it < n; it += G) {
-      const uint32_t sa_i = slot, pa = spar;
-      if (++slot == S) {
-        slot = 0;
-        spar ^= 1u;
-      }
-      uint32_t sb_i = sa_i, pb = pa;
-      if (has_b) {
-        sb_i = slot;
-        pb = spar;
-        if (++slot == S) {
-          slot = 0;
-          spar ^= 1u;
-        }
-      }
-      // Reduction buffer ring: item i uses buffer i % S.  Compute warps write their
-      // partial sums and arrive on redbar (release); the epilogue warp waits on it
+      // Reduction buffer ring: item i uses buffer i % kRedSlots.  Compute warps write
+      // their partial sums and arrive on redbar (release); the epilogue warp waits on it
       // (acquire), sums, marks the buffer free on redfree and runs the item's epilogue.
-      // Compute warps release a slot as soon as their own math is done, never wait for
-      // one another, and only wait for a buffer to be free before reusing it S items on.
+      // Compute warps release the item slot as soon as their own math is done, never
+      // wait for one another, and only wait for a buffer to be free before reusing it.
       if (warp != kEpilogueWarp) {
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        if (ok && !mbar_wait_suspend(&sm.full[slot], spar, deadline)) ok = false;
         if (ok) {
-          ok = mbar_wait_suspend(&sm.full[sa_i], pa, deadline);
-          if (ok && has_b) ok = mbar_wait_suspend(&sm.full[sb_i], pb, deadline);
-        }
-        if (ok) {
-          const uint32_t sa = slot0 + sa_i * slot_bytes, sb = slot0 + sb_i * slot_bytes;
-          if (has_b)
-            item_mma<Op::kFmt, true>(acc, sa, sb, xbase, pl);
-          else
-            item_mma<Op::kFmt, false>(acc, sa, sb, xbase, pl);
+          const uint32_t sa = slot0 + slot * item_bytes;
+          item_mma<Op::kFmt, true>(acc, sa, sa + unit_bytes, xbase, pl);
         }
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&sm.empty[sa_i]);
-          if (has_b) mbar_arrive(&sm.empty[sb_i]);
-        }
-        if (items_done >= S && ok && !mbar_wait_suspend(&sm.redfree[rbuf], rpar ^ 1u, deadline)) ok = false;
-        // pseudo-row grp of A sits at (row grp, column col), of B at (row grp+8, column 4+col)
-        if (t == (pl.col >> 1)) sm.red[rbuf][warp][grp] = (pl.col & 1) ? acc[1] : acc[0];
-        if (t == 2 + (pl.col >> 1)) sm.red[rbuf][warp][8 + grp] = (pl.col & 1) ? acc[3] : acc[2];
+        mbar_arrive_if(&sm.empty[slot], lane == 0);
+        if (items_done >= static_cast<uint32_t>(kRedSlots) && ok &&
+            !mbar_wait_suspend(&sm.redfree[rbuf], rpar ^ 1u, deadline))
+          ok = false;
+        const uint32_t ra = red0 + rbuf * kRedStride;
+        sts_f32_if(ra, odd ? acc[1] : acc[0], st_a);
+        sts_f32_if(ra + 8u * sizeof(float), odd ? acc[3] : acc[2], st_b);
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.redbar[rbuf]);
+        mbar_arrive_if(&sm.redbar[rbuf], lane == 0);
       } else {
         if (ok && !mbar_wait_suspend(&sm.redbar[rbuf], rpar, deadline)) ok = false;
         float v = 0.f;
@@ -502,11 +488,15 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
           for (int w = 0; w < kComputeWarps; ++w) v += sm.red[rbuf][w][lane];
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.redfree[rbuf]);
+        mbar_arrive_if(&sm.redfree[rbuf], lane == 0);
         if (ok) op.item_epilogue(sm, ph, it, lane, v);
       }
+      if (++slot == S) {
+        slot = 0;
+        spar ^= 1u;
+      }
       ++items_done;
-      if (++rbuf == S) {
+      if (++rbuf == static_cast<uint32_t>(kRedSlots)) {
         rbuf = 0;
         rpar ^= 1u;
       }
