@@ -38,6 +38,9 @@ NLAYERS = 4
 # algorithmic bytes of one token (TP1): NVFP4 codes + E4M3 block scales of gate/up/down,
 # three f32 global scales, residual in/out, two norm weights, layer scalar
 WEIGHT_BYTES = 3 * (L * H // 2) + 3 * (L * H // 16)
+MLP_ARGS = ("residual", "pre_ff_rms_weight", "up_weight_packed", "gate_weight_packed", "down_weight_packed",
+            "up_weight_scale", "gate_weight_scale", "down_weight_scale", "up_global_scale", "gate_global_scale",
+            "down_global_scale", "post_ff_rms_weight", "layer_scalar")
 ACT_BYTES = 12 + 2 * H * 2 + 2 * H * 2 + 16
 
 
@@ -169,7 +172,19 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         raise RuntimeError("non-finite residual after warm-up")
 
     # ---------------------------------------------------------------- device-timed region
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    # One round = NLAYERS steps (one per layer).  On one GPU the round is captured once
+    # in a CUDA graph and replayed, so Python's per-call overhead does not gate the
+    # device; consecutive launches overlap through programmatic dependent launch, so the
+    # per-step device time is the timed region / steps.  Steps beyond whole rounds are
+    # launched directly (exactly `steps` launches in total).
+    graph = None
+    if world == 1:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(NLAYERS):
+                step(i)
+        stream.synchronize()
+    rounds, rem = divmod(args.steps, NLAYERS) if graph is not None else (0, args.steps)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
@@ -177,23 +192,35 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     sampler = ClockSampler(local_rank)
     with sampler, torch.cuda.stream(stream):
         t0.record(stream)
-        for i in range(args.steps):
-            evs[i][0].record(stream)
+        for _ in range(rounds):
+            graph.replay()
+        for i in range(rem):
             step(i)
-            evs[i][1].record(stream)
         t1.record(stream)
         stream.synchronize()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     total_ms = t0.elapsed_time(t1)
-    kernel_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+    kernel_ms = total_ms / args.steps
     status = ctx.poll()
+    del graph
 
     # ---------------------------------------------------------------- end to end (host buffers)
+    # What a host program does per token: copy the residual in from pinned host memory,
+    # call the C ABI entry point, copy the result back, wait.  The entry point is bound
+    # to its device buffers once (Context.prepare) and the copies are plain
+    # cudaMemcpyAsync calls on the op's stream.
+    from cuda.bindings import runtime as cudart
+
     host_in = torch.empty(H, dtype=torch.bfloat16, pin_memory=True)
     host_in.copy_(layers[0]["residual"].cpu())
     host_out = torch.empty(H, dtype=torch.bfloat16, pin_memory=True)
+    calls = [ctx.prepare("g4_decoder_feedforward", residual, *[layers[j][k] for k in MLP_ARGS[1:]])
+             for j in range(NLAYERS)]
+    sh = stream.cuda_stream
+    h2d, d2h = cudart.cudaMemcpyKind.cudaMemcpyHostToDevice, cudart.cudaMemcpyKind.cudaMemcpyDeviceToHost
+    dres, hin, hout, nb = residual.data_ptr(), host_in.data_ptr(), host_out.data_ptr(), H * 2
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2e_steps = min(args.steps, 2000)
     if world > 1:
@@ -202,10 +229,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     with torch.cuda.stream(stream):
         e0.record(stream)
         for i in range(e2e_steps):
-            residual.copy_(host_in, non_blocking=True)
-            step(i)
-            host_out.copy_(residual, non_blocking=True)
-            stream.synchronize()
+            cudart.cudaMemcpyAsync(dres, hin, nb, h2d, sh)
+            calls[i % NLAYERS]()
+            cudart.cudaMemcpyAsync(hout, dres, nb, d2h, sh)
+            cudart.cudaStreamSynchronize(sh)
         e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
@@ -229,7 +256,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "config": {"workload": "decoder_feedforward one token, BASELINE config 1 (H=3840, L=15360, NVFP4)",
                    "global_batch": 1, "seq_len": 1, "parallelism": f"tp{world}",
                    "layers_cycled": NLAYERS, "l2": f"inputs larger than L2 ({NLAYERS} layers x "
-                   f"{WEIGHT_BYTES / 1e6:.1f} MB weights cycled per step)"},
+                   f"{WEIGHT_BYTES / 1e6:.1f} MB weights cycled per step)",
+                   "launch": ("CUDA graph of one round (one launch per layer) replayed; consecutive launches "
+                              "overlap via programmatic dependent launch" if world == 1 else
+                              "direct launches + NCCL all-reduce per step")},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                      "traffic": traffic, "algorithmic_bytes_per_launch": algorithmic_bytes(world),

@@ -18,6 +18,38 @@ g4_status check_cuda(g4_ctx* ctx, cudaError_t err, const char* what) {
   if (err == cudaSuccess) return G4_OK;
   return fail(ctx, G4_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
 }
+g4_status launch_kernel(g4_ctx* ctx, const void* fn, dim3 grid, dim3 block, size_t smem, void** args,
+                        bool cooperative, const char* what) {
+  cudaLaunchAttribute attrs[2];
+  unsigned n = 0;
+  if (cooperative) {
+    attrs[n].id = cudaLaunchAttributeCooperative;
+    attrs[n].val.cooperative = 1;
+    ++n;
+  }
+  const unsigned base = n;
+  if (ctx->pdl_ok) {
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = ctx->stream;
+  cfg.attrs = attrs;
+  cfg.numAttrs = n;
+  cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
+  if (e != cudaSuccess && n > base) {
+    (void)cudaGetLastError();
+    ctx->pdl_ok = false;
+    cfg.numAttrs = base;
+    e = cudaLaunchKernelExC(&cfg, fn, args);
+  }
+  return check_cuda(ctx, e, what);
+}
+
 bool aligned16(const void* p) { return p != nullptr && (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // NCCL is resolved at run time, only when tensor parallelism is used: a process that

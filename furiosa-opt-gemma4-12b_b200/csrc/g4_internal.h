@@ -56,6 +56,7 @@ struct g4_ctx {
   g4::DeviceBuffers buf;
   std::string last_error;
   bool coop_ok = true;
+  bool pdl_ok = true;  // programmatic dependent launch accepted by the runtime
 };
 
 namespace g4 {
@@ -71,5 +72,13 @@ g4_status launch_decoder_feedforward(g4_ctx* ctx, uint16_t* residual, const uint
                                      const float* up_gs, const float* gate_gs, const float* down_gs,
                                      const uint16_t* post_w, const uint16_t* layer_scalar);
 g4_status allreduce_f32(g4_ctx* ctx, float* buf, size_t count);
+
+// Launches `fn` on the context's stream, optionally cooperative.  The launch allows
+// programmatic dependent launch: the kernel may start while the previous kernel on the
+// stream finishes, so it must execute griddepcontrol.wait before touching anything that
+// kernel wrote (weights, never written by these kernels, may be read before).  If the
+// runtime rejects that attribute once, the context launches without it from then on.
+g4_status launch_kernel(g4_ctx* ctx, const void* fn, dim3 grid, dim3 block, size_t smem, void** args,
+                        bool cooperative, const char* what);
 
 }  // namespace g4

@@ -1,5 +1,5 @@
 // decoder_feedforward: the NVFP4 GeGLU MLP block of one decode token, ONE persistent
-// cooperative launch (drop-in for ops::decoder_feedforward, src/ops.rs:213-253).
+// launch of one CTA per SM (drop-in for ops::decoder_feedforward, src/ops.rs:213-253).
 //
 //   phase 0  stage:   x = RMSNorm(residual, pre_ff)           (src/device/shared/rmsnorm.rs)
 //   phase 0  items:   8 gate rows + the same 8 up rows per item;
@@ -289,10 +289,14 @@ g4_status launch_decoder_feedforward(g4_ctx* ctx, uint16_t* residual, const uint
   }
   const uint64_t budget = ctx->wait_budget_ns;
   void* args[] = {(void*)&op, (void*)&lay, (void*)&slot_bytes, (void*)&budget};
-  dim3 grid(ctx->sm_count), block(kThreads);
-  g4_status st = check_cuda(
-      ctx, cudaLaunchCooperativeKernel((const void*)mlp_kernel, grid, block, args, lay.total, ctx->stream),
-      "launch mlp_kernel");
+  // Not a cooperative launch, so that the next launch's CTAs can take SMs as this one's
+  // exit (programmatic dependent launch).  The grid barrier between the phases needs
+  // every CTA resident at some point, which holds without the cooperative guarantee:
+  // the grid is one CTA per SM, a CTA's shared memory excludes a second one, and CTAs
+  // waiting at the barrier only wait for SMs held by work that finishes on its own.  Its
+  // bounded wait turns anything else into a device status error, not a hang.
+  g4_status st = launch_kernel(ctx, (const void*)mlp_kernel, dim3(ctx->sm_count), dim3(kThreads), lay.total, args,
+                               false, "launch mlp_kernel");
   if (st != G4_OK) return st;
   if (ctx->tp_world > 1) {
     st = allreduce_f32(ctx, ctx->buf.ybuf, H);

@@ -438,8 +438,9 @@ static g4_status launch_stream(g4_ctx* ctx, const Op& op, uint32_t slot_bytes, u
                             name);
   if (st != G4_OK) return st;
   const int grid = n_items < ctx->sm_count ? n_items : ctx->sm_count;
-  stream_kernel<Op><<<grid, kThreads, lay.total, ctx->stream>>>(op, lay, slot_bytes, ctx->wait_budget_ns);
-  return check_cuda(ctx, cudaGetLastError(), name);
+  uint64_t budget = ctx->wait_budget_ns;
+  void* args[] = {(void*)&op, (void*)&lay, (void*)&slot_bytes, (void*)&budget};
+  return launch_kernel(ctx, (const void*)stream_kernel<Op>, dim3(grid), dim3(kThreads), lay.total, args, false, name);
 }
 
 // ---------------------------------------------------------------------------- launchers

@@ -392,6 +392,9 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
     fence_mbar_init();
   }
   __syncthreads();
+  // The next launch may start taking SMs as this grid's CTAs exit; before its
+  // griddepcontrol.wait it only streams weights and prefetches, which no kernel writes.
+  pdl_launch_dependents();
 
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------------------ producer
@@ -437,6 +440,9 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
   // The epilogue warp is idle until the first item completes: it pulls the operands of
   // the op's final epilogue into L2 now, so the last CTA's tail finds them there.
   if (warp == kEpilogueWarp) op.prefetch_tail(cta, lane);
+  // Everything below may read what the previous kernel on the stream wrote (activations,
+  // residual, this context's scratch counters and buffers).
+  pdl_wait();
   uint32_t slot = 0, spar = 0;                 // next item slot to consume, its fill parity
   uint32_t rbuf = 0, rpar = 0, items_done = 0; // reduction buffer ring
   bool ok = true;

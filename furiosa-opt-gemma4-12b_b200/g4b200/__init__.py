@@ -149,6 +149,23 @@ class Context:
         f = getattr(LIB, fn)
         self._check(fn, f(self.handle, *[(_ptr(a) if not isinstance(a, (ctypes._SimpleCData,)) else a) for a in args]))
 
+    def prepare(self, fn: str, *args):
+        """Bind `g4_<op>` (e.g. "g4_decoder_feedforward") to these tensors once and return a
+        zero-argument callable that issues it, for host loops that launch the same op on
+        the same buffers many times.  The arguments are converted here, not per call, and
+        not shape-checked: run the op once through its checked wrapper first."""
+        f = getattr(LIB, fn)
+        keep = list(args)  # the tensors must outlive the callable
+        cargs = [self.handle] + [a if isinstance(a, ctypes._SimpleCData) else _vp(_ptr(a)) for a in args]
+
+        def call() -> None:
+            code = f(*cargs)
+            if code != 0:
+                self._check(fn, code)
+
+        call.args = keep
+        return call
+
     def set_wait_budget(self, timeout_us: int) -> None:
         self._check("g4_ctx_set_wait_budget", LIB.g4_ctx_set_wait_budget(self.handle, timeout_us))
 
