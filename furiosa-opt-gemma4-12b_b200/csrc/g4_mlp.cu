@@ -101,6 +101,7 @@ struct MlpOp {
       // h and its max were published before the grid barrier (acquired by its thread 0,
       // then bar.sync): plain L2 loads, 8 h values per 16-byte load, all issued together.
       constexpr int kG = 4;  // lrows <= kG * 8 * kConsumerThreads
+      static_assert(kG * 8 * kConsumerThreads >= L, "phase-1 staging must cover L");
       uint4 hv[kG];
 #pragma unroll
       for (int k = 0; k < kG; ++k) {

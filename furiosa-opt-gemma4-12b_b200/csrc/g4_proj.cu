@@ -243,7 +243,8 @@ struct OprojOp {
   // 8 inputs per 16-byte load, all loads issued first (K <= kG * 8 * kConsumerThreads).
   __device__ void stage(StreamSmem& sm, uint8_t* xbuf, int, int tid, const XLayout& xl) const {
     uint16_t* xs = reinterpret_cast<uint16_t*>(xbuf);
-    constexpr int kG = 2;
+    constexpr int kG = 3;
+    static_assert(kG * 8 * kConsumerThreads >= 8192, "o-proj staging must cover K = Qf");
     uint4 xv[kG];
     float rs[kG];
 #pragma unroll

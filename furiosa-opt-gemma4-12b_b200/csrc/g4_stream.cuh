@@ -14,15 +14,16 @@
 // different columns walk the K chunks in rotated order, so the two rows one 8-lane
 // shared-memory phase reads never share banks.
 //
-// Pipeline.  One producer thread streams units into a ring of shared-memory SLOTS with
-// 1-D bulk copies (`cp.async.bulk`, L2 evict-first): one copy for a unit's codes and one
-// for its block scales, completing on the slot's "full" mbarrier.  NW consumer warps
-// split each item's K chunks, decode weights in registers (E2M1 -> f16 with
-// `cvt.rn.f16x2.e2m1x2`, times the E4M3 block scale: exact in f16; E4M3 -> f16 exact;
-// bf16 as is), accumulate in f32 on the tensor cores, release the slot on its "empty"
-// mbarrier and reduce their partial dot products through shared memory; one consumer
-// warp per item runs the op's epilogue.  CTAs are persistent (one per SM), taking items
-// round robin.
+// Pipeline.  A producer warp streams items into a ring of shared-memory item SLOTS with
+// 1-D bulk copies (`cp.async.bulk`, L2 evict-first): per unit one copy of its codes and
+// one of its block scales, all four of an item completing on the slot's "full" mbarrier.
+// The compute warps split each item's K chunks, decode weights in registers (E2M1 -> f16
+// with `cvt.rn.f16x2.e2m1x2`, times the E4M3 block scale: exact in f16; E4M3 -> f16
+// exact; bf16 as is), accumulate in f32 on the tensor cores, release the slot on its
+// "empty" mbarrier and leave their partial dot products in a shared-memory reduction
+// buffer; a couple of items later one of them (in rotation) adds the partials up and runs
+// the op's epilogue for the item.  CTAs are persistent (one per SM), taking items round
+// robin.
 //
 // Activations are staged in shared memory as f16 scaled by 2^e (e from the vector's max
 // magnitude), so f16 x f16 products are exact in f32 and the scale is undone exactly in
@@ -61,28 +62,32 @@ __host__ __device__ inline UnitGeom make_geom(Fmt f, uint32_t rb, uint32_t q) {
   return g;
 }
 
-// Warp roles: kComputeWarps compute warps (0 .. kComputeWarps-1), one epilogue warp
-// (kComputeWarps), one producer warp (kComputeWarps+1).  "Consumer" threads = compute +
-// epilogue warps: they stage activations and run the final epilogue together.
+// Warp roles: kComputeWarps compute warps (0 .. kComputeWarps-1) and one producer warp
+// (kComputeWarps).  The compute warps ("consumers") also stage activations, run the item
+// epilogues (item j by warp j % kComputeWarps, kEpiLag items after contracting it) and
+// the final epilogue.  Sixteen warps keep four per scheduler, so a thread may use 128
+// registers; the decode/MMA loop needs about 110 to run without stalls.
 #ifndef G4_COMPUTE_WARPS
 #define G4_COMPUTE_WARPS 15
 #endif
 constexpr int kComputeWarps = G4_COMPUTE_WARPS;
-constexpr int kEpilogueWarp = kComputeWarps;
-constexpr int kConsumerWarps = kComputeWarps + 1;
+constexpr int kConsumerWarps = kComputeWarps;
+constexpr uint32_t kEpiLag = 2;  // items between contracting an item and running its epilogue
 constexpr int kMaxSlots = 8;       // unit slots of a launch's layout (two per item slot)
 constexpr int kRedSlots = 8;       // reduction buffers (ring over items)
 constexpr int kProducerLanes = 4;  // issuing lanes; item slots = a multiple of this
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr uint32_t kBarConsumers = 1;  // named barrier id among consumer warps
+// the vectorised staging and tails give each consumer thread 8 elements of a [3840] vector
+static_assert(kConsumerThreads * 8 >= 3840, "too few consumer threads for an [H] vector");
 
 // Shared-memory header of a streaming kernel (the x buffer and the slots follow).
 struct StreamSmem {
   uint64_t full[kMaxSlots / 2];               // item slot filled (both units landed)
   uint64_t empty[kMaxSlots / 2];              // every compute warp is done with the item slot
   uint64_t redbar[kRedSlots];                 // all compute warps wrote the buffer's partials
-  uint64_t redfree[kRedSlots];                // the epilogue warp has read the buffer
+  uint64_t redfree[kRedSlots];                // the item's epilogue has read the buffer
   float red[kRedSlots][kComputeWarps][16];    // per-item partial sums, ring of buffers
   float scratch[64];        // op-defined (norm reductions, flags)
   int xexp;                 // activation scale exponent: x16 = x * 2^xexp
@@ -108,13 +113,14 @@ __host__ __device__ inline StreamLayout make_layout(uint32_t slot_bytes, uint32_
   return l;
 }
 
-// Chunks (64 code bytes of every pseudo-row) one compute warp handles per item, at most.
-constexpr int kMaxChunks = 3;
+// Chunks (64 code bytes of every pseudo-row) one compute warp handles per item, at most:
+// enough for pseudo-rows of up to 45 chunks (2880 bytes).
+constexpr int kMaxChunks = (45 + kComputeWarps - 1) / kComputeWarps;
 
 // Host-side check of a unit geometry against the strides a launch will use.
 __host__ inline bool geom_ok(const UnitGeom& g, uint32_t code_stride, uint32_t scale_stride) {
   const bool contiguous = code_stride == g.q * g.rb && (g.sb == 0 || scale_stride == g.q * g.sb);
-  return g.rb % 64u == 0 && g.rb / 64u <= static_cast<uint32_t>(kMaxChunks * kComputeWarps) &&
+  return g.rb % 64u == 0 && g.rb / 64u <= 45u &&
          (g.q == 1 || g.q == 2 || g.q == 4) && contiguous && (8u * g.sb) % 16u == 0;
 }
 
@@ -362,7 +368,7 @@ __device__ __forceinline__ void item_mma(float (&acc)[4], uint32_t sa, uint32_t 
 //   bool has_final(); void final_epilogue(StreamSmem&, uint8_t* xbuf, int tid) [last CTA]
 //   uint32_t* done_counter(); uint32_t* status();
 //   bool between_phases(StreamSmem&, int phase, uint64_t deadline)  [consumer threads]
-//   void prefetch_tail(int cta, int lane)   [epilogue warp, at start: L2 prefetches]
+//   void prefetch_tail(int cta, int lane)   [producer warp, at start: L2 prefetches]
 // `unit_bytes` is the launch's unit slot size (>= every phase's 8 * (rb + sb), a multiple
 // of 128); lay.nslots unit slots form lay.nslots / 2 item slots.
 template <class Op>
@@ -396,11 +402,14 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
   // griddepcontrol.wait it only streams weights and prefetches, which no kernel writes.
   pdl_launch_dependents();
 
-  if (warp == kConsumerWarps) {
+  if (warp == kComputeWarps) {
     // ------------------------------------------------------------------ producer
+    // First pull the operands of the op's final epilogue into L2 (all lanes), so the
+    // last CTA's tail finds them there.
     // kProducerLanes lanes issue in parallel.  Every lane walks the same item sequence
     // k = 0, 1, ...; lane j issues the items k with k % kProducerLanes == j, into item
     // slots j, j + kProducerLanes, ... (k % S), counting its own refills of them.
+    op.prefetch_tail(cta, lane);
     if (lane < kProducerLanes) {
       const uint64_t pol = l2_evict_first_policy();
       uint32_t k = 0, s = static_cast<uint32_t>(lane), use = 0, mine = 0;
@@ -437,20 +446,31 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
   }
 
   // -------------------------------------------------------------------- consumers
-  // The epilogue warp is idle until the first item completes: it pulls the operands of
-  // the op's final epilogue into L2 now, so the last CTA's tail finds them there.
-  if (warp == kEpilogueWarp) op.prefetch_tail(cta, lane);
   // Everything below may read what the previous kernel on the stream wrote (activations,
   // residual, this context's scratch counters and buffers).
   pdl_wait();
-  uint32_t slot = 0, spar = 0;                 // next item slot to consume, its fill parity
-  uint32_t rbuf = 0, rpar = 0, items_done = 0; // reduction buffer ring
+  uint32_t slot = 0, spar = 0;  // next item slot to consume, its fill parity
+  uint32_t done = 0;            // items this CTA has contracted, all phases (reduction ring index)
   bool ok = true;
   const int grp = lane >> 2, t = lane & 3;
   const uint32_t xbase = smem_u32(xbuf), slot0 = smem_u32(slots);
-  // this lane's slot in every reduction buffer (compute warps)
-  const uint32_t red0 = smem_u32(&sm.red[0][warp < kComputeWarps ? warp : 0][grp]);
+  const uint32_t red0 = smem_u32(&sm.red[0][warp][grp]);  // this lane's slot in reduction buffer 0
   constexpr uint32_t kRedStride = sizeof(float) * kComputeWarps * 16;
+  // Epilogue of this CTA's item j (global index; m = its index within phase ph): wait
+  // until every compute warp wrote its partial sums, add them in fixed warp order, free
+  // the buffer, run the op's epilogue.  Item j uses reduction buffer j % kRedSlots.
+  auto epilogue = [&](int ph, uint32_t j, uint32_t m) {
+    const uint32_t rb = j % kRedSlots, rp = (j / kRedSlots) & 1u;
+    if (ok && !mbar_wait_suspend(&sm.redbar[rb], rp, deadline)) ok = false;
+    float v = 0.f;
+    if (lane < 16) {
+#pragma unroll
+      for (int w = 0; w < kComputeWarps; ++w) v += sm.red[rb][w][lane];
+    }
+    __syncwarp();
+    mbar_arrive_if(&sm.redfree[rb], lane == 0);
+    if (ok) op.item_epilogue(sm, ph, cta + static_cast<int>(m) * G, lane, v);
+  };
   for (int ph = 0; ph < Op::kPhases; ++ph) {
     if (ph > 0) {
       if (!op.between_phases(sm, ph, deadline)) ok = false;
@@ -460,54 +480,47 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
     named_bar_sync(kBarConsumers, kConsumerThreads);
     if (sm.failed) ok = false;
     const int n = op.items(ph);
+    const uint32_t count = (cta < n) ? static_cast<uint32_t>((n - cta + G - 1) / G) : 0u;
+    const uint32_t first = done;
     const LanePlan pl = make_plan<Op::kFmt>(g, warp, lane, true);
     // pseudo-row grp of A sits at (row grp, column col), of B at (row grp+8, column 4+col)
     const bool st_a = t == (pl.col >> 1), st_b = t == 2 + (pl.col >> 1), odd = (pl.col & 1) != 0;
-    for (int it = cta; it < n; it += G) {
-      // Reduction buffer ring: item i uses buffer i % kRedSlots.  Compute warps write
-      // their partial sums and arrive on redbar (release); the epilogue warp waits on it
-      // (acquire), sums, marks the buffer free on redfree and runs the item's epilogue.
-      // Compute warps release the item slot as soon as their own math is done, never
-      // wait for one another, and only wait for a buffer to be free before reusing it.
-      if (warp != kEpilogueWarp) {
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        if (ok && !mbar_wait_suspend(&sm.full[slot], spar, deadline)) ok = false;
-        if (ok) {
-          const uint32_t sa = slot0 + slot * item_bytes;
-          item_mma<Op::kFmt, true>(acc, sa, sa + unit_bytes, xbase, pl);
-        }
-        __syncwarp();
-        mbar_arrive_if(&sm.empty[slot], lane == 0);
-        if (items_done >= static_cast<uint32_t>(kRedSlots) && ok &&
-            !mbar_wait_suspend(&sm.redfree[rbuf], rpar ^ 1u, deadline))
-          ok = false;
-        const uint32_t ra = red0 + rbuf * kRedStride;
-        sts_f32_if(ra, odd ? acc[1] : acc[0], st_a);
-        sts_f32_if(ra + 8u * sizeof(float), odd ? acc[3] : acc[2], st_b);
-        __syncwarp();
-        mbar_arrive_if(&sm.redbar[rbuf], lane == 0);
-      } else {
-        if (ok && !mbar_wait_suspend(&sm.redbar[rbuf], rpar, deadline)) ok = false;
-        float v = 0.f;
-        if (lane < 16) {
-#pragma unroll
-          for (int w = 0; w < kComputeWarps; ++w) v += sm.red[rbuf][w][lane];
-        }
-        __syncwarp();
-        mbar_arrive_if(&sm.redfree[rbuf], lane == 0);
-        if (ok) op.item_epilogue(sm, ph, it, lane, v);
+    for (uint32_t m = 0; m < count; ++m) {
+      // Compute warps release the item slot as soon as their own math is done, never wait
+      // for one another, and only wait for a reduction buffer to be free before reusing it.
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      if (ok && !mbar_wait_suspend(&sm.full[slot], spar, deadline)) ok = false;
+      if (ok) {
+        const uint32_t sa = slot0 + slot * item_bytes;
+        item_mma<Op::kFmt, true>(acc, sa, sa + unit_bytes, xbase, pl);
       }
+      __syncwarp();
+      mbar_arrive_if(&sm.empty[slot], lane == 0);
       if (++slot == S) {
         slot = 0;
         spar ^= 1u;
       }
-      ++items_done;
-      if (++rbuf == static_cast<uint32_t>(kRedSlots)) {
-        rbuf = 0;
-        rpar ^= 1u;
+      const uint32_t rb = done % kRedSlots;
+      if (done >= static_cast<uint32_t>(kRedSlots) && ok &&
+          !mbar_wait_suspend(&sm.redfree[rb], ((done / kRedSlots) & 1u) ^ 1u, deadline))
+        ok = false;
+      const uint32_t ra = red0 + rb * kRedStride;
+      sts_f32_if(ra, odd ? acc[1] : acc[0], st_a);
+      sts_f32_if(ra + 8u * sizeof(float), odd ? acc[3] : acc[2], st_b);
+      __syncwarp();
+      mbar_arrive_if(&sm.redbar[rb], lane == 0);
+      ++done;
+      if (m >= kEpiLag) {
+        const uint32_t j = done - 1u - kEpiLag;
+        if (j % kComputeWarps == static_cast<uint32_t>(warp)) epilogue(ph, j, m - kEpiLag);
       }
     }
-    if (!ok && tid == 0) atomicOr(op.status(), DEV_ERR_TIMEOUT_MBAR);
+    // the phase's last kEpiLag epilogues, before anything reads its results
+    for (uint32_t m = (count > kEpiLag ? count - kEpiLag : 0u); m < count; ++m) {
+      const uint32_t j = first + m;
+      if (j % kComputeWarps == static_cast<uint32_t>(warp)) epilogue(ph, j, m);
+    }
+    if (!ok) atomicOr(op.status(), DEV_ERR_TIMEOUT_MBAR);
   }
 
   if (op.has_final()) {
@@ -526,7 +539,8 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
   }
 }
 
-// Sum of the q pseudo-row values of each real row of a unit, in the epilogue warp:
+// Sum of the q pseudo-row values of each real row of a unit, in the warp running the
+// item's epilogue:
 // lane l (< 8/q) receives real row l of unit A, lane 8/q + l real row l of unit B.
 // Lanes hold v = pseudo-row values (0-7: A, 8-15: B); the sum order is fixed.
 __device__ __forceinline__ float sum_pseudo_rows(float v, int lane, int q) {
