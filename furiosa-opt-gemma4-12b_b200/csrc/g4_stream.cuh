@@ -86,8 +86,6 @@ static_assert(kConsumerThreads * 8 >= 3840, "too few consumer threads for an [H]
 struct StreamSmem {
   uint64_t full[kMaxSlots / 2];               // item slot filled (both units landed)
   uint64_t empty[kMaxSlots / 2];              // every compute warp is done with the item slot
-  uint64_t redbar[kRedSlots];                 // all compute warps wrote the buffer's partials
-  uint64_t redfree[kRedSlots];                // the item's epilogue has read the buffer
   float red[kRedSlots][kComputeWarps][16];    // per-item partial sums, ring of buffers
   float scratch[64];        // op-defined (norm reductions, flags)
   int xexp;                 // activation scale exponent: x16 = x * 2^xexp
@@ -389,10 +387,6 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], kComputeWarps);
     }
-    for (int s = 0; s < kRedSlots; ++s) {
-      mbar_init(&sm.redbar[s], kComputeWarps);
-      mbar_init(&sm.redfree[s], 1);
-    }
     sm.is_last = 0;
     sm.failed = 0;
     fence_mbar_init();
@@ -456,19 +450,24 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
   const uint32_t xbase = smem_u32(xbuf), slot0 = smem_u32(slots);
   const uint32_t red0 = smem_u32(&sm.red[0][warp][grp]);  // this lane's slot in reduction buffer 0
   constexpr uint32_t kRedStride = sizeof(float) * kComputeWarps * 16;
-  // Epilogue of this CTA's item j (global index; m = its index within phase ph): wait
-  // until every compute warp wrote its partial sums, add them in fixed warp order, free
-  // the buffer, run the op's epilogue.  Item j uses reduction buffer j % kRedSlots.
+  // Epilogue of this CTA's item j (global index; m = its index within phase ph).  Item j
+  // sits in item slot j % S and leaves its partial sums in reduction buffer j % kRedSlots;
+  // every compute warp writes its partials before it arrives on the slot's "empty"
+  // barrier (a release), so that barrier's completion for item j (phase j / S) also says
+  // "all partials are in".  Add them in fixed warp order and run the op's epilogue.
+  // Buffers need no "free" signal: item j + kRedSlots writes buffer j % kRedSlots only
+  // after item j + kRedSlots - S was released by every warp, and the warp running item
+  // j's epilogue does so before it contracts item j + kEpiLag + 1 <= j + kRedSlots - S.
+  static_assert(kRedSlots >= kMaxSlots / 2 + static_cast<int>(kEpiLag) + 1, "reduction ring too short");
   auto epilogue = [&](int ph, uint32_t j, uint32_t m) {
-    const uint32_t rb = j % kRedSlots, rp = (j / kRedSlots) & 1u;
-    if (ok && !mbar_wait_suspend(&sm.redbar[rb], rp, deadline)) ok = false;
+    const uint32_t rb = j % kRedSlots;
+    if (ok && !mbar_wait_suspend(&sm.empty[j % S], (j / S) & 1u, deadline)) ok = false;
     float v = 0.f;
     if (lane < 16) {
 #pragma unroll
       for (int w = 0; w < kComputeWarps; ++w) v += sm.red[rb][w][lane];
     }
     __syncwarp();
-    mbar_arrive_if(&sm.redfree[rb], lane == 0);
     if (ok) op.item_epilogue(sm, ph, cta + static_cast<int>(m) * G, lane, v);
   };
   for (int ph = 0; ph < Op::kPhases; ++ph) {
@@ -486,29 +485,23 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
     // pseudo-row grp of A sits at (row grp, column col), of B at (row grp+8, column 4+col)
     const bool st_a = t == (pl.col >> 1), st_b = t == 2 + (pl.col >> 1), odd = (pl.col & 1) != 0;
     for (uint32_t m = 0; m < count; ++m) {
-      // Compute warps release the item slot as soon as their own math is done, never wait
-      // for one another, and only wait for a reduction buffer to be free before reusing it.
+      // Compute warps write their partial sums, then release the item slot (one arrive
+      // per warp), and never wait for one another.
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
       if (ok && !mbar_wait_suspend(&sm.full[slot], spar, deadline)) ok = false;
       if (ok) {
         const uint32_t sa = slot0 + slot * item_bytes;
         item_mma<Op::kFmt, true>(acc, sa, sa + unit_bytes, xbase, pl);
       }
+      const uint32_t ra = red0 + (done % kRedSlots) * kRedStride;
+      sts_f32_if(ra, odd ? acc[1] : acc[0], st_a);
+      sts_f32_if(ra + 8u * sizeof(float), odd ? acc[3] : acc[2], st_b);
       __syncwarp();
       mbar_arrive_if(&sm.empty[slot], lane == 0);
       if (++slot == S) {
         slot = 0;
         spar ^= 1u;
       }
-      const uint32_t rb = done % kRedSlots;
-      if (done >= static_cast<uint32_t>(kRedSlots) && ok &&
-          !mbar_wait_suspend(&sm.redfree[rb], ((done / kRedSlots) & 1u) ^ 1u, deadline))
-        ok = false;
-      const uint32_t ra = red0 + rb * kRedStride;
-      sts_f32_if(ra, odd ? acc[1] : acc[0], st_a);
-      sts_f32_if(ra + 8u * sizeof(float), odd ? acc[3] : acc[2], st_b);
-      __syncwarp();
-      mbar_arrive_if(&sm.redbar[rb], lane == 0);
       ++done;
       if (m >= kEpiLag) {
         const uint32_t j = done - 1u - kEpiLag;
