@@ -74,14 +74,16 @@ struct MlpOp {
   }
   __device__ uint32_t* status() const { return &scr->status; }
   __device__ uint32_t* done_counter() const { return &scr->mlp_done; }
-  // The fused tail reads post_w, layer_scalar and down_gs once, in the last CTA: CTA c
-  // pulls line c of post_w (and CTA 0 the scalars) into L2 at kernel start.
-  __device__ void prefetch_tail(int cta, int lane) const {
-    if (ybuf != nullptr) return;  // TP: the tail runs in its own kernel after the all-reduce
+  // At kernel start CTA c pulls line c of the pre-FF norm weight (read by every CTA's
+  // staging) and, for the fused tail, line c of post_w (CTA 0: the scalars) into L2.
+  __device__ void prefetch_l2(int cta, int lane) const {
     constexpr int kBytes = H * 2, kLines = kBytes / 128 + 1;
-    const uint8_t* pw = reinterpret_cast<const uint8_t*>(post_w);
-    if (lane == 0 && cta < kLines) prefetch_l2_keep(pw + min(cta * 128, kBytes - 1));
-    if (lane == 1 && cta == 0) {
+    if (cta >= kLines) return;
+    const int off = min(cta * 128, kBytes - 1);
+    if (lane == 0) prefetch_l2_keep(reinterpret_cast<const uint8_t*>(pre_w) + off);
+    if (ybuf != nullptr) return;  // TP: the tail runs in its own kernel after the all-reduce
+    if (lane == 1) prefetch_l2_keep(reinterpret_cast<const uint8_t*>(post_w) + off);
+    if (lane == 2 && cta == 0) {
       prefetch_l2_keep(layer_scalar);
       prefetch_l2_keep(down_gs);
     }

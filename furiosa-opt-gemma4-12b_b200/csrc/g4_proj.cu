@@ -85,7 +85,11 @@ struct QkvOp {
   __device__ bool has_final() const { return false; }
   __device__ bool between_phases(StreamSmem&, int, uint64_t) const { return true; }
   __device__ void final_epilogue(StreamSmem&, uint8_t*, int) const {}
-  __device__ void prefetch_tail(int, int) const {}
+  // CTA c pulls line c of the input norm weight (read by every CTA's staging) into L2.
+  __device__ void prefetch_l2(int cta, int lane) const {
+    constexpr int kBytes = H * 2, kLines = kBytes / 128 + 1;
+    if (lane == 0 && cta < kLines) prefetch_l2_keep(reinterpret_cast<const uint8_t*>(in_w) + min(cta * 128, kBytes - 1));
+  }
   __device__ void stage(StreamSmem& sm, uint8_t* xbuf, int, int tid, const XLayout& xl) const {
     const int e = stage_rmsnorm(x, in_w, H, reinterpret_cast<uint16_t*>(xbuf), true, sm.scratch, xl);
     if (tid == 0) sm.xexp = e;
@@ -225,9 +229,9 @@ struct OprojOp {
   }
   __device__ uint32_t* status() const { return &scr->status; }
   __device__ uint32_t* done_counter() const { return &scr->proj_done; }
-  // The fused tail (last CTA) reads residual, post_w and the row scales: CTA c pulls line
+  // The fused tail (CTA 0) reads residual, post_w and the row scales: CTA c pulls line
   // c of each into L2 at kernel start.
-  __device__ void prefetch_tail(int cta, int lane) const {
+  __device__ void prefetch_l2(int cta, int lane) const {
     if (ybuf != nullptr) return;  // TP: the tail runs in its own kernel after the all-reduce
     constexpr int kBytes = H * 2, kLines = kBytes / 128 + 1;
     if (cta >= kLines) return;
@@ -399,7 +403,11 @@ struct LmHeadOp {
   __device__ bool has_final() const { return false; }
   __device__ bool between_phases(StreamSmem&, int, uint64_t) const { return true; }
   __device__ void final_epilogue(StreamSmem&, uint8_t*, int) const {}
-  __device__ void prefetch_tail(int, int) const {}
+  // CTA c pulls line c of the final norm weight (read by every CTA's staging) into L2.
+  __device__ void prefetch_l2(int cta, int lane) const {
+    constexpr int kBytes = H * 2, kLines = kBytes / 128 + 1;
+    if (lane == 0 && cta < kLines) prefetch_l2_keep(reinterpret_cast<const uint8_t*>(w_norm) + min(cta * 128, kBytes - 1));
+  }
   __device__ void stage(StreamSmem& sm, uint8_t* xbuf, int, int tid, const XLayout& xl) const {
     stage_rmsnorm(x, w_norm, H, reinterpret_cast<uint16_t*>(xbuf), false, sm.scratch, xl);
     if (tid == 0) sm.xexp = 0;

@@ -89,7 +89,6 @@ struct StreamSmem {
   float red[kRedSlots][kComputeWarps][16];    // per-item partial sums, ring of buffers
   float scratch[64];        // op-defined (norm reductions, flags)
   int xexp;                 // activation scale exponent: x16 = x * 2^xexp
-  int is_last;              // this CTA completed the launch (runs the final epilogue)
   int failed;               // a bounded wait gave up
   int pad_;
 };
@@ -363,10 +362,11 @@ __device__ __forceinline__ void item_mma(float (&acc)[4], uint32_t sa, uint32_t 
 //   void stage(StreamSmem&, uint8_t* xbuf, int phase, int tid, const XLayout&)  [consumers]
 //   void item_epilogue(StreamSmem&, int phase, int item, int lane, float v)  [one warp]
 //       lanes 0-7: pseudo-rows of unit A, lanes 8-15: pseudo-rows of unit B
-//   bool has_final(); void final_epilogue(StreamSmem&, uint8_t* xbuf, int tid) [last CTA]
+//   bool has_final(); void final_epilogue(StreamSmem&, uint8_t* xbuf, int tid) [CTA 0, after all]
 //   uint32_t* done_counter(); uint32_t* status();
 //   bool between_phases(StreamSmem&, int phase, uint64_t deadline)  [consumer threads]
-//   void prefetch_tail(int cta, int lane)   [producer warp, at start: L2 prefetches]
+//   void prefetch_l2(int cta, int lane)   [producer warp, at start: L2 prefetches of the
+//       staging and final-epilogue operands that no kernel writes]
 // `unit_bytes` is the launch's unit slot size (>= every phase's 8 * (rb + sb), a multiple
 // of 128); lay.nslots unit slots form lay.nslots / 2 item slots.
 template <class Op>
@@ -387,7 +387,6 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], kComputeWarps);
     }
-    sm.is_last = 0;
     sm.failed = 0;
     fence_mbar_init();
   }
@@ -398,12 +397,12 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
 
   if (warp == kComputeWarps) {
     // ------------------------------------------------------------------ producer
-    // First pull the operands of the op's final epilogue into L2 (all lanes), so the
-    // last CTA's tail finds them there.
+    // First pull the staging and final-epilogue operands that no kernel writes (norm
+    // weights, scales) into L2 (all lanes), so the staging and the tail find them there.
     // kProducerLanes lanes issue in parallel.  Every lane walks the same item sequence
     // k = 0, 1, ...; lane j issues the items k with k % kProducerLanes == j, into item
     // slots j, j + kProducerLanes, ... (k % S), counting its own refills of them.
-    op.prefetch_tail(cta, lane);
+    op.prefetch_l2(cta, lane);
     if (lane < kProducerLanes) {
       const uint64_t pol = l2_evict_first_policy();
       uint32_t k = 0, s = static_cast<uint32_t>(lane), use = 0, mine = 0;
@@ -517,18 +516,30 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
   }
 
   if (op.has_final()) {
+    // CTA 0 runs the final epilogue once every other CTA has published its results: they
+    // each add 1 to the done counter (release, no round trip) and exit; CTA 0 polls it
+    // (acquire) right after its own items, while the others finish.
     named_bar_sync(kBarConsumers, kConsumerThreads);
+    if (cta != 0) {
+      if (tid == 0) red_add_release_gpu(op.done_counter(), 1u);
+      return;
+    }
     if (tid == 0) {
-      // acq_rel: releases this CTA's partial sums, and in the last CTA acquires everyone's
-      const uint32_t old = atom_add_acq_rel_gpu(op.done_counter(), 1u);
-      sm.is_last = (old == static_cast<uint32_t>(G - 1)) ? 1 : 0;
+      uint32_t spins = 0;
+      int fail = 0;
+      while (ld_acquire_gpu(op.done_counter()) < static_cast<uint32_t>(G - 1)) {
+        if ((++spins & 63u) == 0u && global_ns() > deadline) {
+          fail = 1;
+          atomicOr(op.status(), DEV_ERR_TIMEOUT_GRID);
+          break;
+        }
+      }
+      sm.failed = fail;
     }
     named_bar_sync(kBarConsumers, kConsumerThreads);
-    if (sm.is_last) {
-      op.final_epilogue(sm, xbuf, tid);
-      named_bar_sync(kBarConsumers, kConsumerThreads);
-      if (tid == 0) *op.done_counter() = 0u;  // visible to the next launch at kernel end
-    }
+    if (!sm.failed) op.final_epilogue(sm, xbuf, tid);
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+    if (tid == 0) *op.done_counter() = 0u;  // visible to the next launch at kernel end
   }
 }
 
@@ -596,6 +607,26 @@ __device__ __forceinline__ float consumer_max(float v, float* scratch) {
   return s;
 }
 
+// Block-wide (consumer threads) sum of `s` and max of `m` in one barrier round, for the
+// first reduction of a launch (nothing reads scratch[0..63] concurrently).
+__device__ __forceinline__ float2 consumer_sum_max(float s, float m, float* scratch) {
+  s = warp_sum(s);
+  m = warp_max(m);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    scratch[warp] = s;
+    scratch[32 + warp] = m;
+  }
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  float ts = 0.f, tm = 0.f;
+#pragma unroll
+  for (int w = 0; w < kConsumerWarps; ++w) {
+    ts += scratch[w];
+    tm = fmaxf(tm, scratch[32 + w]);
+  }
+  return make_float2(ts, tm);
+}
+
 // RMSNorm of a bf16 vector (global) into shared memory as scaled f16 (or bf16) MMA
 // operands, by the consumer threads.  Returns the scale exponent (0 for bf16 output).
 __device__ __forceinline__ int stage_rmsnorm(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
@@ -604,7 +635,7 @@ __device__ __forceinline__ int stage_rmsnorm(const uint16_t* __restrict__ x, con
   const int tid = threadIdx.x;
   constexpr int kMaxGroups = 2;  // n <= 2 * 8 * kConsumerThreads
   uint4 xv[kMaxGroups], wv[kMaxGroups];
-  float ss = 0.f;
+  float ss = 0.f, pm = 0.f;  // sum of x^2; max |x * w|
 #pragma unroll
   for (int k = 0; k < kMaxGroups; ++k) {
     const int gi = tid + k * kConsumerThreads;
@@ -612,18 +643,23 @@ __device__ __forceinline__ int stage_rmsnorm(const uint16_t* __restrict__ x, con
       xv[k] = __ldg(reinterpret_cast<const uint4*>(x) + gi);
       wv[k] = __ldg(reinterpret_cast<const uint4*>(w) + gi);
       const uint32_t xw[4] = {xv[k].x, xv[k].y, xv[k].z, xv[k].w};
+      const uint32_t ww[4] = {wv[k].x, wv[k].y, wv[k].z, wv[k].w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float a = bf16_to_f32(static_cast<uint16_t>(xw[i] & 0xFFFFu));
         const float b = bf16_to_f32(static_cast<uint16_t>(xw[i] >> 16));
         ss = __fadd_rn(ss, __fmul_rn(a, a));
         ss = __fadd_rn(ss, __fmul_rn(b, b));
+        pm = fmaxf(pm, fabsf(a * bf16_to_f32(static_cast<uint16_t>(ww[i] & 0xFFFFu))));
+        pm = fmaxf(pm, fabsf(b * bf16_to_f32(static_cast<uint16_t>(ww[i] >> 16))));
       }
     }
   }
-  const float r = rms_factor(consumer_sum(ss, scratch), n);
+  // One reduction round for both: the f16 scale only needs an upper bound of max |y|,
+  // and |y| = |bf16(x * r * w)| <= max|x * w| * r * (1 + 2^-7).
+  const float2 red = consumer_sum_max(ss, pm, scratch);
+  const float r = rms_factor(red.x, n);
   float y[kMaxGroups][8];
-  float amax = 0.f;
 #pragma unroll
   for (int k = 0; k < kMaxGroups; ++k) {
     const int gi = tid + k * kConsumerThreads;
@@ -635,14 +671,13 @@ __device__ __forceinline__ int stage_rmsnorm(const uint16_t* __restrict__ x, con
         const uint16_t xb = static_cast<uint16_t>((i & 1) ? xw[i >> 1] >> 16 : xw[i >> 1] & 0xFFFFu);
         const uint16_t wb = static_cast<uint16_t>((i & 1) ? ww[i >> 1] >> 16 : ww[i >> 1] & 0xFFFFu);
         y[k][i] = round_bf16(__fmul_rn(__fmul_rn(bf16_to_f32(xb), r), bf16_to_f32(wb)));
-        amax = fmaxf(amax, fabsf(y[k][i]));
       }
     }
   }
   int e = 0;
   float sc = 1.0f;
   if (as_f16) {
-    e = f16_scale_exponent(consumer_max(amax, scratch + 32));
+    e = f16_scale_exponent(red.y * r * 1.01f);
     sc = ldexpf(1.0f, e);
   }
 #pragma unroll
