@@ -3,7 +3,10 @@
 #include <nccl.h>
 
 #include <cstring>
+#include <mutex>
+#include <set>
 #include <string>
+#include <utility>
 
 #include "g4_internal.h"
 #include "g4_common.cuh"
@@ -18,6 +21,21 @@ g4_status check_cuda(g4_ctx* ctx, cudaError_t err, const char* what) {
   if (err == cudaSuccess) return G4_OK;
   return fail(ctx, G4_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
 }
+g4_status allow_max_dynamic_smem(g4_ctx* ctx, const void* fn, size_t need, const char* what) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({fn, ctx->device})) return G4_OK;
+  int optin = 0;
+  g4_status st = check_cuda(ctx, cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device),
+                            "cudaDeviceGetAttribute(smem opt-in)");
+  if (st != G4_OK) return st;
+  if (need > static_cast<size_t>(optin)) return fail(ctx, G4_ERR_UNSUPPORTED, std::string(what) + ": shared memory layout too large");
+  st = check_cuda(ctx, cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin), what);
+  if (st == G4_OK) done.insert({fn, ctx->device});
+  return st;
+}
+
 g4_status launch_kernel(g4_ctx* ctx, const void* fn, dim3 grid, dim3 block, size_t smem, void** args,
                         bool cooperative, const char* what) {
   cudaLaunchAttribute attrs[2];

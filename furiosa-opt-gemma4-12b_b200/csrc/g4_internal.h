@@ -73,6 +73,11 @@ g4_status launch_decoder_feedforward(g4_ctx* ctx, uint16_t* residual, const uint
                                      const uint16_t* post_w, const uint16_t* layer_scalar);
 g4_status allreduce_f32(g4_ctx* ctx, float* buf, size_t count);
 
+// Raises `fn`'s dynamic shared-memory limit to the device's opt-in maximum, once per
+// (kernel, device): every launch, whatever its layout (`need` bytes, checked), then fits,
+// and no context can lower the limit under another.
+g4_status allow_max_dynamic_smem(g4_ctx* ctx, const void* fn, size_t need, const char* what);
+
 // Launches `fn` on the context's stream, optionally cooperative.  The launch allows
 // programmatic dependent launch: the kernel may start while the previous kernel on the
 // stream finishes, so it must execute griddepcontrol.wait before touching anything that

@@ -282,13 +282,9 @@ g4_status launch_decoder_feedforward(g4_ctx* ctx, uint16_t* residual, const uint
   // activation buffer: h as f16 (phase 1) or the f32 down-projection sums (final epilogue)
   const uint32_t x_bytes = static_cast<uint32_t>(op.lrows * 2 > H * 4 ? op.lrows * 2 : H * 4);
   const StreamLayout lay = make_layout(slot_bytes, kMlpSlots, x_bytes);
-  static bool attr_set[16] = {};
-  if (!attr_set[ctx->device & 15]) {
-    g4_status st = check_cuda(ctx, cudaFuncSetAttribute(mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                        static_cast<int>(lay.total)),
-                              "cudaFuncSetAttribute(mlp)");
+  {
+    const g4_status st = allow_max_dynamic_smem(ctx, (const void*)mlp_kernel, lay.total, "mlp_kernel smem");
     if (st != G4_OK) return st;
-    attr_set[ctx->device & 15] = true;
   }
   const uint64_t budget = ctx->wait_budget_ns;
   void* args[] = {(void*)&op, (void*)&lay, (void*)&slot_bytes, (void*)&budget};

@@ -441,10 +441,7 @@ template <class Op>
 static g4_status launch_stream(g4_ctx* ctx, const Op& op, uint32_t slot_bytes, uint32_t nslots, uint32_t x_bytes,
                                int n_items, const char* name) {
   const StreamLayout lay = make_layout(slot_bytes, nslots, x_bytes);
-  g4_status st = check_cuda(ctx,
-                            cudaFuncSetAttribute(stream_kernel<Op>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 static_cast<int>(lay.total)),
-                            name);
+  g4_status st = allow_max_dynamic_smem(ctx, (const void*)stream_kernel<Op>, lay.total, name);
   if (st != G4_OK) return st;
   const int grid = n_items < ctx->sm_count ? n_items : ctx->sm_count;
   uint64_t budget = ctx->wait_budget_ns;
