@@ -172,19 +172,19 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         raise RuntimeError("non-finite residual after warm-up")
 
     # ---------------------------------------------------------------- device-timed region
-    # One round = NLAYERS steps (one per layer).  On one GPU the round is captured once
-    # in a CUDA graph and replayed, so Python's per-call overhead does not gate the
-    # device; consecutive launches overlap through programmatic dependent launch, so the
+    # One round = NLAYERS steps (one per layer).  The round is captured once in a CUDA
+    # graph and replayed, so Python's per-call overhead does not gate the device;
+    # consecutive launches overlap through programmatic dependent launch, so the
     # per-step device time is the timed region / steps.  Steps beyond whole rounds are
-    # launched directly (exactly `steps` launches in total).
-    graph = None
-    if world == 1:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            for i in range(NLAYERS):
-                step(i)
-        stream.synchronize()
-    rounds, rem = divmod(args.steps, NLAYERS) if graph is not None else (0, args.steps)
+    # launched directly (exactly `steps` launches in total).  Under TP the all-reduce
+    # runs inside the kernel over peer memory, so the graph holds no NCCL call (on the
+    # NCCL fallback it does, and is released before the process group).
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(NLAYERS):
+            step(i)
+    stream.synchronize()
+    rounds, rem = divmod(args.steps, NLAYERS)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
@@ -241,6 +241,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     ms_per_step, kernel_ms, e2e_ms = vals.tolist()
+    peer = ctx.tp_peer_exchange
     ctx.close()
     if rank != 0:
         return None
@@ -257,16 +258,18 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                    "global_batch": 1, "seq_len": 1, "parallelism": f"tp{world}",
                    "layers_cycled": NLAYERS, "l2": f"inputs larger than L2 ({NLAYERS} layers x "
                    f"{WEIGHT_BYTES / 1e6:.1f} MB weights cycled per step)",
-                   "launch": ("CUDA graph of one round (one launch per layer) replayed; consecutive launches "
-                              "overlap via programmatic dependent launch" if world == 1 else
-                              "direct launches + NCCL all-reduce per step")},
+                   "launch": "CUDA graph of one round (one launch per layer) replayed; consecutive launches "
+                             "overlap via programmatic dependent launch" + (
+                                 "" if world == 1 else
+                                 "; TP all-reduce inside the kernel over NVLink peer memory" if peer else
+                                 "; TP all-reduce by NCCL, then a one-CTA epilogue kernel")},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                      "traffic": traffic, "algorithmic_bytes_per_launch": algorithmic_bytes(world),
                      "kernel_us": round(kernel_ms * 1000.0, 3)},
         "e2e": {"value": round(e2e_ms * 1000.0, 3), "unit": UNIT, "h2d_bytes_per_step": H * 2,
                 "d2h_bytes_per_step": H * 2},
-        "gpu_launches": args.steps * (1 if world == 1 else 2),
+        "gpu_launches": args.steps * (1 if world == 1 or peer else 2),
         "clocks": sampler.summary(),
         "device_status": status,
     }

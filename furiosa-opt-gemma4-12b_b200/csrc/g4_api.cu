@@ -2,6 +2,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <set>
@@ -79,6 +80,7 @@ struct NcclApi {
   ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                              cudaStream_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
 };
@@ -94,9 +96,11 @@ static NcclApi& nccl() {
   api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
   api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
   api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+  api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
   api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
   api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
-  api.ok = api.get_unique_id && api.comm_init_rank && api.all_reduce && api.comm_destroy && api.error_string;
+  api.ok = api.get_unique_id && api.comm_init_rank && api.all_reduce && api.all_gather && api.comm_destroy &&
+           api.error_string;
   return api;
 }
 
@@ -105,6 +109,80 @@ g4_status allreduce_f32(g4_ctx* ctx, float* buf, size_t count) {
   const ncclResult_t r =
       nccl().all_reduce(buf, buf, count, ncclFloat32, ncclSum, reinterpret_cast<ncclComm_t>(ctx->comm), ctx->stream);
   if (r != ncclSuccess) return fail(ctx, G4_ERR_NCCL, std::string("ncclAllReduce: ") + nccl().error_string(r));
+  return G4_OK;
+}
+
+// Maps every rank's TP exchange buffer into this process (CUDA IPC handles swapped with
+// an NCCL all-gather), so that the MLP and o-proj kernels all-reduce their partial
+// outputs themselves over NVLink.  The ranks then agree (NCCL min) on whether all of
+// them succeeded: any rank without peer access, or with G4B200_TP_EXCHANGE=nccl in its
+// environment, puts every rank on the NCCL all-reduce path instead.  Returns G4_OK in
+// both cases; an error only if the NCCL calls themselves fail.
+static void close_peer_exchange(g4_ctx* ctx) {
+  for (int p = 0; p < kMaxTp; ++p) {
+    if (ctx->peers.buf[p] != nullptr && p != ctx->tp_rank) cudaIpcCloseMemHandle(ctx->peers.buf[p]);
+    ctx->peers.buf[p] = nullptr;
+  }
+  ctx->peers.world = 0;
+}
+
+static g4_status setup_peer_exchange(g4_ctx* ctx) {
+  const int world = ctx->tp_world, rank = ctx->tp_rank;
+  const ncclComm_t comm = reinterpret_cast<ncclComm_t>(ctx->comm);
+  const char* env = std::getenv("G4B200_TP_EXCHANGE");
+  bool ok = !(env != nullptr && std::strcmp(env, "nccl") == 0);
+  cudaIpcMemHandle_t mine = {};
+  if (ok) ok = cudaMalloc(&ctx->buf.xch, kXchBytes) == cudaSuccess;
+  if (ok) ok = cudaMemset(ctx->buf.xch, 0, kXchBytes) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
+  if (ok) ok = cudaIpcGetMemHandle(&mine, ctx->buf.xch) == cudaSuccess;
+  if (!ok) (void)cudaGetLastError();
+  // [world] handles gathered in the row-parallel partial buffer (unused until the first
+  // launch), then the agreement flag after them
+  static_assert(sizeof(cudaIpcMemHandle_t) * kMaxTp + 4 <= kPartFloats * 4, "staging fits");
+  uint8_t* stage = reinterpret_cast<uint8_t*>(ctx->buf.part);
+  const size_t hb = sizeof(cudaIpcMemHandle_t);
+  // (a pageable host-to-device copy may return before its DMA lands: synchronize before
+  // NCCL reads it on another stream)
+  g4_status st = check_cuda(ctx, cudaMemcpy(stage + rank * hb, &mine, hb, cudaMemcpyHostToDevice), "xch: stage");
+  if (st == G4_OK) st = check_cuda(ctx, cudaDeviceSynchronize(), "xch: stage sync");
+  if (st != G4_OK) return st;
+  ncclResult_t r = nccl().all_gather(stage + rank * hb, stage, hb, ncclUint8, comm, ctx->stream);
+  if (r != ncclSuccess) return fail(ctx, G4_ERR_NCCL, std::string("ncclAllGather: ") + nccl().error_string(r));
+  cudaIpcMemHandle_t all[kMaxTp];
+  st = check_cuda(ctx, cudaStreamSynchronize(ctx->stream), "xch: gather");
+  if (st == G4_OK) st = check_cuda(ctx, cudaMemcpy(all, stage, hb * world, cudaMemcpyDeviceToHost), "xch: read");
+  if (st != G4_OK) return st;
+  ctx->peers = PeerXch{};
+  for (int p = 0; p < world && ok; ++p) {
+    if (p == rank) {
+      ctx->peers.buf[p] = ctx->buf.xch;
+      continue;
+    }
+    void* ptr = nullptr;
+    if (cudaIpcOpenMemHandle(&ptr, all[p], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      (void)cudaGetLastError();
+      ok = false;
+    } else {
+      ctx->peers.buf[p] = static_cast<uint64_t*>(ptr);
+    }
+  }
+  int32_t* flag = reinterpret_cast<int32_t*>(stage + hb * kMaxTp);
+  const int32_t mine_ok = ok ? 1 : 0;
+  int32_t all_ok = 0;
+  st = check_cuda(ctx, cudaMemcpy(flag, &mine_ok, 4, cudaMemcpyHostToDevice), "xch: flag");
+  if (st == G4_OK) st = check_cuda(ctx, cudaDeviceSynchronize(), "xch: flag sync");
+  if (st != G4_OK) return st;
+  r = nccl().all_reduce(flag, flag, 1, ncclInt32, ncclMin, comm, ctx->stream);
+  if (r != ncclSuccess) return fail(ctx, G4_ERR_NCCL, std::string("ncclAllReduce: ") + nccl().error_string(r));
+  st = check_cuda(ctx, cudaStreamSynchronize(ctx->stream), "xch: agree");
+  if (st == G4_OK) st = check_cuda(ctx, cudaMemcpy(&all_ok, flag, 4, cudaMemcpyDeviceToHost), "xch: agree read");
+  if (st != G4_OK) return st;
+  if (all_ok == 1) {
+    ctx->peers.rank = rank;
+    ctx->peers.world = world;
+  } else {
+    close_peer_exchange(ctx);
+  }
   return G4_OK;
 }
 
@@ -189,6 +267,7 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
 g4_status g4_ctx_destroy(g4_ctx* ctx) {
   G4_CHECK_CTX(ctx);
   cudaSetDevice(ctx->device);
+  close_peer_exchange(ctx);
   if (ctx->comm && nccl().ok) nccl().comm_destroy(reinterpret_cast<ncclComm_t>(ctx->comm));
   cudaFree(ctx->buf.scratch);
   cudaFree(ctx->buf.part);
@@ -196,6 +275,7 @@ g4_status g4_ctx_destroy(g4_ctx* ctx) {
   cudaFree(ctx->buf.hbuf);
   cudaFree(ctx->buf.ybuf);
   cudaFree(ctx->buf.attn);
+  cudaFree(ctx->buf.xch);
   delete ctx;
   return G4_OK;
 }
@@ -231,6 +311,12 @@ g4_status g4_ctx_init_tp(g4_ctx* ctx, int rank, int world, const uint8_t nccl_id
   const ncclResult_t r = nccl().comm_init_rank(&comm, world, id, rank);
   if (r != ncclSuccess) return fail(ctx, G4_ERR_NCCL, std::string("ncclCommInitRank: ") + nccl().error_string(r));
   ctx->comm = reinterpret_cast<ncclComm*>(comm);
+  return setup_peer_exchange(ctx);
+}
+
+g4_status g4_ctx_tp_peer_exchange(const g4_ctx* ctx, int* out_enabled) {
+  if (ctx == nullptr || out_enabled == nullptr) return G4_ERR_BAD_ARG;
+  *out_enabled = ctx->peers.world > 1 ? 1 : 0;
   return G4_OK;
 }
 

@@ -22,7 +22,8 @@ struct Scratch {
   uint32_t mlp_amax;          // MLP: bits of max |h| over the intermediate vector
   uint32_t proj_done;         // o-proj: CTAs done
   uint32_t lm_done;           // (reserved)
-  uint32_t pad0[2];
+  uint32_t xch_epoch;         // TP: launches that used the peer exchange (same on every rank)
+  uint32_t pad0;
   uint32_t head_count[64];    // qkv: completed items per head group
   uint32_t attn_count[64];    // split-KV attention: completed chunks per kv head
   uint32_t attn_done;         // paged attention: CTAs done
@@ -34,6 +35,23 @@ constexpr size_t kHeadFloats = 8192 + 512 + 8192; // raw projection rows (qkv)
 constexpr size_t kHFloats = 15360;                // MLP intermediate (bf16 stored)
 constexpr size_t kAttnFloats = 512 * (2 * 16 + 16 * 512) + 4096;  // 512 chunks of 16 heads
 
+// Tensor-parallel one-shot all-reduce over peer memory.  Each rank owns one exchange
+// buffer of 64-bit words, word[2][kMaxTp][3840]: two halves used by alternate launches,
+// one [3840] slot per source rank.  A word carries one f32 value (low half) and the
+// number of the launch that sent it (high half), so a reader knows a value has arrived
+// without any fence or separate flag.
+constexpr int kMaxTp = 8;
+constexpr size_t kXchWords = 2 * static_cast<size_t>(kMaxTp) * 3840;
+constexpr size_t kXchBytes = kXchWords * 8;
+
+// This rank's view of every rank's exchange buffer (its own included); world <= 1 means
+// the peer exchange is not in use.
+struct PeerXch {
+  uint64_t* buf[kMaxTp];
+  int rank;
+  int world;
+};
+
 struct DeviceBuffers {
   Scratch* scratch = nullptr;
   float* part = nullptr;     // [kPartFloats]
@@ -41,6 +59,7 @@ struct DeviceBuffers {
   uint16_t* hbuf = nullptr;  // [kHFloats] bf16
   float* ybuf = nullptr;     // [3840] f32 (TP all-reduce buffer)
   float* attn = nullptr;     // [kAttnFloats] split-KV partials
+  uint64_t* xch = nullptr;   // [kXchWords] TP peer exchange (this rank's, IPC-exported)
 };
 
 }  // namespace g4
@@ -57,6 +76,7 @@ struct g4_ctx {
   std::string last_error;
   bool coop_ok = true;
   bool pdl_ok = true;  // programmatic dependent launch accepted by the runtime
+  g4::PeerXch peers = {};  // TP exchange buffers mapped from every rank (world 0: NCCL path)
 };
 
 namespace g4 {

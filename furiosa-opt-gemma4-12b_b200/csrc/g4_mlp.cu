@@ -15,8 +15,10 @@
 //
 // The producer warp never waits for the grid: it streams phase-1 down weights while the
 // last gate/up items of other CTAs finish, so the phase boundary costs no HBM time.
-// Under tensor parallelism the last CTA instead writes the f32 partial y, which the
-// host all-reduces before the norm epilogue kernel.
+// Under tensor parallelism CTA 0 first sums the ranks' partial y in a one-shot
+// all-reduce over NVLink peer memory (peer_allreduce), then runs the same tail on the
+// full vector; without peer access the partial y goes to an NCCL all-reduce and a
+// one-CTA epilogue kernel instead.
 #include <mutex>
 
 #include "g4_internal.h"
@@ -44,7 +46,8 @@ struct MlpOp {
   Scratch* scr;
   float* part;
   uint16_t* hbuf;
-  float* ybuf;      // TP: f32 partial y for the all-reduce (nullptr: fused epilogue)
+  float* ybuf;      // TP over NCCL: f32 partial y for the all-reduce (nullptr: fused tail)
+  PeerXch xch;      // TP over peer memory (world <= 1: not in use)
   int lrows;        // local intermediate rows (L / tp)
   int dq;           // down: K segments per row (pseudo-rows per real row)
   UnitGeom g0, g1;  // gate/up: 8 rows x 3840 K; down: 8/dq rows x full K
@@ -174,7 +177,7 @@ struct MlpOp {
         reinterpret_cast<float4*>(ybuf)[2 * tid] = make_float4(y[0], y[1], y[2], y[3]);
         reinterpret_cast<float4*>(ybuf)[2 * tid + 1] = make_float4(y[4], y[5], y[6], y[7]);
       }
-    } else {
+    } else if (xch.world <= 1 || peer_allreduce(xch, &scr->xch_epoch, y, tid, &scr->status, sm)) {
       const float gsd = __ldg(down_gs);
       float ss = 0.f;
       if (mine) {
@@ -270,7 +273,9 @@ g4_status launch_decoder_feedforward(g4_ctx* ctx, uint16_t* residual, const uint
   op.scr = ctx->buf.scratch;
   op.part = ctx->buf.part;
   op.hbuf = ctx->buf.hbuf;
-  op.ybuf = ctx->tp_world > 1 ? ctx->buf.ybuf : nullptr;
+  const bool tp_nccl = ctx->tp_world > 1 && ctx->peers.world <= 1;
+  op.ybuf = tp_nccl ? ctx->buf.ybuf : nullptr;
+  op.xch = ctx->peers;
   op.lrows = L / ctx->tp_world;
   // down rows hold lrows K elements: cut into dq segments of 3840 (one segment when smaller)
   op.dq = (op.lrows % 3840 == 0) ? op.lrows / 3840 : 1;
@@ -297,7 +302,7 @@ g4_status launch_decoder_feedforward(g4_ctx* ctx, uint16_t* residual, const uint
   g4_status st = launch_kernel(ctx, (const void*)mlp_kernel, dim3(ctx->sm_count), dim3(kThreads), lay.total, args,
                                false, "launch mlp_kernel");
   if (st != G4_OK) return st;
-  if (ctx->tp_world > 1) {
+  if (tp_nccl) {
     st = allreduce_f32(ctx, ctx->buf.ybuf, H);
     if (st != G4_OK) return st;
     mlp_tp_epilogue_kernel<<<1, 1024, 0, ctx->stream>>>(ctx->buf.ybuf, down_gs, post_w, layer_scalar, residual);
@@ -426,6 +431,7 @@ extern "C" g4_status g4_decoder_feedforward_noalloc(
   op.part = reinterpret_cast<float*>(d.base + kNoAllocPartOff);
   op.hbuf = reinterpret_cast<uint16_t*>(d.base + kNoAllocHOff);
   op.ybuf = nullptr;
+  op.xch = PeerXch{};
 
   // The opt-in maximum, never lower: the context path sets this attribute once per
   // device for its own (possibly larger) layout and must keep working after us.

@@ -210,7 +210,8 @@ struct OprojOp {
   uint16_t* residual;
   Scratch* scr;
   float* part;
-  float* ybuf;      // TP: partial y (already unscaled) for the all-reduce
+  float* ybuf;      // TP over NCCL: partial y (already unscaled) for the all-reduce
+  PeerXch xch;      // TP over peer memory (world <= 1: not in use)
   UnitGeom g;
 
   // a unit is 8/q whole output rows; an item two units (A, B)
@@ -317,6 +318,7 @@ struct OprojOp {
       }
       return;
     }
+    if (xch.world > 1 && !peer_allreduce(xch, &scr->xch_epoch, y, tid, &scr->status, sm)) return;
     const float gs = nvfp4 ? __ldg(gsc) : 0.f;
     const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
     float ss = 0.f;
@@ -515,7 +517,9 @@ g4_status launch_oproj(g4_ctx* ctx, bool full, bool nvfp4, const uint16_t* x, co
   op.residual = residual;
   op.scr = ctx->buf.scratch;
   op.part = ctx->buf.part;
-  op.ybuf = tp > 1 ? ctx->buf.ybuf : nullptr;
+  const bool tp_nccl = tp > 1 && ctx->peers.world <= 1;
+  op.ybuf = tp_nccl ? ctx->buf.ybuf : nullptr;
+  op.xch = ctx->peers;
   const uint32_t rowbytes = nvfp4 ? op.K / 2 : op.K;
   op.g = make_geom(nvfp4 ? Fmt::NVFP4 : Fmt::FP8, rowbytes / op.q, op.q);
   if (!geom_ok(op.g, rowbytes, op.K / 16)) return fail(ctx, G4_ERR_UNSUPPORTED, "o-proj geometry");
@@ -531,7 +535,7 @@ g4_status launch_oproj(g4_ctx* ctx, bool full, bool nvfp4, const uint16_t* x, co
     static_cast<OprojOp&>(o) = op;
     st = launch_stream(ctx, o, op.g.slot_bytes, 8, xb, n_items, "oproj_fp8");
   }
-  if (st != G4_OK || tp == 1) return st;
+  if (st != G4_OK || !tp_nccl) return st;
   st = allreduce_f32(ctx, ctx->buf.ybuf, H);
   if (st != G4_OK) return st;
   oproj_tp_epilogue_kernel<<<1, 1024, 0, ctx->stream>>>(ctx->buf.ybuf, op.nvfp4, row_scale, gsc, post_w, residual);

@@ -31,6 +31,7 @@
 #pragma once
 
 #include "g4_common.cuh"
+#include "g4_internal.h"
 
 namespace g4 {
 
@@ -86,6 +87,7 @@ static_assert(kConsumerThreads * 8 >= 3840, "too few consumer threads for an [H]
 struct StreamSmem {
   uint64_t full[kMaxSlots / 2];               // item slot filled (both units landed)
   uint64_t empty[kMaxSlots / 2];              // every compute warp is done with the item slot
+  uint64_t deadline;                          // global_ns() limit of the launch's bounded waits
   float red[kRedSlots][kComputeWarps][16];    // per-item partial sums, ring of buffers
   float scratch[64];        // op-defined (norm reductions, flags)
   int xexp;                 // activation scale exponent: x16 = x * 2^xexp
@@ -388,6 +390,7 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
       mbar_init(&sm.empty[s], kComputeWarps);
     }
     sm.failed = 0;
+    sm.deadline = deadline;
     fence_mbar_init();
   }
   __syncthreads();
@@ -580,6 +583,71 @@ __device__ __forceinline__ bool grid_wait(uint32_t* counter, uint32_t target, ui
     sm.failed = fail;
   }
   named_bar_sync(kBarConsumers, kConsumerThreads);
+  return sm.failed == 0;
+}
+
+// Tensor parallelism: one-shot all-reduce of an [H] f32 vector over peer memory, run by
+// all consumer threads of the CTA doing the final epilogue.  Thread tid < H/8 holds
+// elements [8 tid, 8 tid + 8) of this rank's partial in y and receives the sum over all
+// ranks, added in rank order so that every rank computes the identical vector.  Each
+// value goes to its slot in every rank's exchange buffer as one 64-bit word {value,
+// launch number}; the reader polls its own words until all carry this launch's number.
+// An 8-byte store is seen whole or not at all, so neither a fence nor a flag is needed.
+// The half of the buffer alternates with the launch number: a rank one launch ahead
+// never overwrites words a peer still reads, and cannot get two ahead, because it needs
+// that peer's words of the launch in between.  Returns false (and sets
+// DEV_ERR_TIMEOUT_PEER) if a peer's values do not arrive before the launch's deadline.
+__device__ __forceinline__ bool peer_allreduce(const PeerXch& x, uint32_t* launch_ctr, float (&y)[8], int tid,
+                                               uint32_t* status, StreamSmem& sm) {
+  constexpr int kH = 3840;
+  if (tid == 0) {
+    sm.scratch[63] = __uint_as_float(*launch_ctr + 1u);
+    sm.failed = 0;
+  }
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  const uint32_t e = __float_as_uint(sm.scratch[63]);
+  if (tid < kH / 8) {
+    const uint64_t tag = static_cast<uint64_t>(e) << 32;
+    const size_t half = static_cast<size_t>(e & 1u) * kMaxTp * kH;
+    uint64_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w[i] = tag | __float_as_uint(y[i]);
+    for (int p = 0; p < x.world; ++p) {
+      uint64_t* dst = x.buf[p] + half + static_cast<size_t>(x.rank) * kH + 8 * tid;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) st_relaxed_sys_v2u64(dst + 2 * j, w[2 * j], w[2 * j + 1]);
+    }
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    bool ok = true;
+    for (int q = 0; q < x.world && ok; ++q) {
+      const uint64_t* src = x.buf[x.rank] + half + static_cast<size_t>(q) * kH + 8 * tid;
+      uint64_t v[8];
+      uint32_t spins = 0;
+      while (true) {
+        bool all = true;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          ld_relaxed_sys_v2u64(src + 2 * j, v[2 * j], v[2 * j + 1]);
+          all = all && static_cast<uint32_t>(v[2 * j] >> 32) == e && static_cast<uint32_t>(v[2 * j + 1] >> 32) == e;
+        }
+        if (all) break;
+        if ((++spins & 255u) == 0u && global_ns() > sm.deadline) {
+          ok = false;
+          break;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += __uint_as_float(static_cast<uint32_t>(v[i]));
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = acc[i];
+    if (!ok) {
+      sm.failed = 1;
+      atomicOr(status, DEV_ERR_TIMEOUT_PEER);
+    }
+  }
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  if (tid == 0) *launch_ctr = e;
   return sm.failed == 0;
 }
 

@@ -71,6 +71,7 @@ LIB.g4_ctx_set_wait_budget.argtypes = [_vp, _u32]
 LIB.g4_ctx_poll_device_status.argtypes = [_vp, ctypes.POINTER(_u32)]
 LIB.g4_nccl_unique_id.argtypes = [ctypes.c_char_p]
 LIB.g4_ctx_init_tp.argtypes = [_vp, _i32, _i32, ctypes.c_char_p]
+LIB.g4_ctx_tp_peer_exchange.argtypes = [_vp, ctypes.POINTER(ctypes.c_int)]
 
 
 def header_symbols() -> list[str]:
@@ -165,6 +166,14 @@ class Context:
 
         call.args = keep
         return call
+
+    @property
+    def tp_peer_exchange(self) -> bool:
+        """True if this rank's MLP / o-proj kernels all-reduce over NVLink peer memory
+        (False: the NCCL fallback, or not tensor-parallel)."""
+        out = ctypes.c_int(0)
+        self._check("g4_ctx_tp_peer_exchange", LIB.g4_ctx_tp_peer_exchange(self.handle, ctypes.byref(out)))
+        return bool(out.value)
 
     def set_wait_budget(self, timeout_us: int) -> None:
         self._check("g4_ctx_set_wait_budget", LIB.g4_ctx_set_wait_budget(self.handle, timeout_us))

@@ -90,9 +90,20 @@ g4_status g4_ctx_set_stream(g4_ctx* ctx, g4_stream_t stream);
  * `nccl_id` points to the 128-byte ncclUniqueId rank 0 created (g4_nccl_unique_id)
  * and broadcast out of band.  After this, projection entry points take this rank's
  * weight shard (column-parallel gate/up/q/k/v rows, row-parallel down/o K-slices)
- * and all-reduce the row-parallel partial sums before their RMSNorm epilogue. */
+ * and all-reduce the row-parallel partial sums before their RMSNorm epilogue.
+ * The all-reduce runs inside the MLP / o-proj kernel over NVLink peer memory: each
+ * rank's exchange buffer (480 KiB) is mapped into every other rank's process with
+ * CUDA IPC, so the ranks must be separate processes with peer access.  Otherwise, or
+ * when any rank has G4B200_TP_EXCHANGE=nccl in its environment, every rank agrees to
+ * use an NCCL all-reduce and a separate epilogue kernel instead.  The ranks must issue
+ * the same sequence of MLP / o-proj calls, and destroy their contexts only after all
+ * ranks' launches have finished.  (The reference runs on one chip and has no
+ * counterpart; src/lib.rs:17.) */
 g4_status g4_nccl_unique_id(uint8_t out_id[128]);
 g4_status g4_ctx_init_tp(g4_ctx* ctx, int rank, int world, const uint8_t nccl_id[128]);
+/* 1 if this context's MLP / o-proj kernels all-reduce over peer memory, 0 if they use
+ * the NCCL fallback or the context is not tensor-parallel.  No reference counterpart. */
+g4_status g4_ctx_tp_peer_exchange(const g4_ctx* ctx, int* out_enabled);
 /* Message of the last failing call on this context (never NULL). */
 const char* g4_ctx_last_error(const g4_ctx* ctx);
 /* Time limit, in microseconds, of every bounded device-side wait (mbarrier, grid-wide
