@@ -31,8 +31,14 @@ g4_status allow_max_dynamic_smem(g4_ctx* ctx, const void* fn, size_t need, const
   g4_status st = check_cuda(ctx, cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device),
                             "cudaDeviceGetAttribute(smem opt-in)");
   if (st != G4_OK) return st;
-  if (need > static_cast<size_t>(optin)) return fail(ctx, G4_ERR_UNSUPPORTED, std::string(what) + ": shared memory layout too large");
-  st = check_cuda(ctx, cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin), what);
+  // the opt-in maximum covers static and dynamic shared memory together
+  cudaFuncAttributes fa = {};
+  st = check_cuda(ctx, cudaFuncGetAttributes(&fa, fn), "cudaFuncGetAttributes");
+  if (st != G4_OK) return st;
+  const int dyn_max = optin - static_cast<int>(fa.sharedSizeBytes);
+  if (dyn_max <= 0 || need > static_cast<size_t>(dyn_max))
+    return fail(ctx, G4_ERR_UNSUPPORTED, std::string(what) + ": shared memory layout too large");
+  st = check_cuda(ctx, cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn_max), what);
   if (st == G4_OK) done.insert({fn, ctx->device});
   return st;
 }
@@ -255,6 +261,9 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   if (st == G4_OK) st = check_cuda(ctx, cudaMalloc(&b.hbuf, kHFloats * 2), "cudaMalloc hbuf");
   if (st == G4_OK) st = check_cuda(ctx, cudaMalloc(&b.ybuf, 3840 * 4), "cudaMalloc ybuf");
   if (st == G4_OK) st = check_cuda(ctx, cudaMalloc(&b.attn, kAttnFloats * 4), "cudaMalloc attn");
+  if (st == G4_OK) st = check_cuda(ctx, cudaMalloc(&b.tc_seg, kTcSegFloats * 4), "cudaMalloc tc_seg");
+  if (st == G4_OK) st = check_cuda(ctx, cudaMalloc(&b.tc_cnt, kTcTiles * 4), "cudaMalloc tc_cnt");
+  if (st == G4_OK) st = check_cuda(ctx, cudaMemset(b.tc_cnt, 0, kTcTiles * 4), "cudaMemset tc_cnt");
   if (st == G4_OK) st = check_cuda(ctx, cudaDeviceSynchronize(), "ctx init");
   if (st != G4_OK) {
     g4_ctx_destroy(ctx);
@@ -276,6 +285,8 @@ g4_status g4_ctx_destroy(g4_ctx* ctx) {
   cudaFree(ctx->buf.ybuf);
   cudaFree(ctx->buf.attn);
   cudaFree(ctx->buf.xch);
+  cudaFree(ctx->buf.tc_seg);
+  cudaFree(ctx->buf.tc_cnt);
   delete ctx;
   return G4_OK;
 }
@@ -326,6 +337,14 @@ g4_status g4_ctx_set_wait_budget(g4_ctx* ctx, uint32_t timeout_us) {
   G4_CHECK_CTX(ctx);
   if (timeout_us == 0) return fail(ctx, G4_ERR_BAD_ARG, "wait budget must be positive");
   ctx->wait_budget_ns = static_cast<uint64_t>(timeout_us) * 1000ull;
+  return G4_OK;
+}
+
+g4_status g4_ctx_set_mlp_kernel(g4_ctx* ctx, int kind) {
+  G4_CHECK_CTX(ctx);
+  if (kind != G4_MLP_AUTO && kind != G4_MLP_STREAM && kind != G4_MLP_TENSOR)
+    return fail(ctx, G4_ERR_BAD_ARG, "mlp kernel must be G4_MLP_AUTO, G4_MLP_STREAM or G4_MLP_TENSOR");
+  ctx->mlp_kernel = kind;
   return G4_OK;
 }
 

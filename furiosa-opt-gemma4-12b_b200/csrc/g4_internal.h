@@ -34,6 +34,8 @@ constexpr size_t kPartFloats = 16 * 3840 * 2;     // row-parallel partial sums
 constexpr size_t kHeadFloats = 8192 + 512 + 8192; // raw projection rows (qkv)
 constexpr size_t kHFloats = 15360;                // MLP intermediate (bf16 stored)
 constexpr size_t kAttnFloats = 512 * (2 * 16 + 16 * 512) + 4096;  // 512 chunks of 16 heads
+constexpr size_t kTcTiles = 15360 / 64 + 3840 / 128;              // gate/up tiles + down tiles
+constexpr size_t kTcSegFloats = kTcTiles * 8 * 128;               // 8 segment slots of 128 rows
 
 // Tensor-parallel one-shot all-reduce over peer memory.  Each rank owns one exchange
 // buffer of 64-bit words, word[2][kMaxTp][3840]: two halves used by alternate launches,
@@ -60,6 +62,8 @@ struct DeviceBuffers {
   float* ybuf = nullptr;     // [3840] f32 (TP all-reduce buffer)
   float* attn = nullptr;     // [kAttnFloats] split-KV partials
   uint64_t* xch = nullptr;   // [kXchWords] TP peer exchange (this rank's, IPC-exported)
+  float* tc_seg = nullptr;   // [kTcSegFloats] tensor-core MLP: per-tile segment partials
+  uint32_t* tc_cnt = nullptr;  // [kTcTiles] tensor-core MLP: segments finished per tile (zero between launches)
 };
 
 }  // namespace g4
@@ -76,6 +80,7 @@ struct g4_ctx {
   std::string last_error;
   bool coop_ok = true;
   bool pdl_ok = true;  // programmatic dependent launch accepted by the runtime
+  int mlp_kernel = 0;  // G4_MLP_AUTO / G4_MLP_STREAM / G4_MLP_TENSOR
   g4::PeerXch peers = {};  // TP exchange buffers mapped from every rank (world 0: NCCL path)
 };
 
@@ -92,6 +97,12 @@ g4_status launch_decoder_feedforward(g4_ctx* ctx, uint16_t* residual, const uint
                                      const float* up_gs, const float* gate_gs, const float* down_gs,
                                      const uint16_t* post_w, const uint16_t* layer_scalar);
 g4_status allreduce_f32(g4_ctx* ctx, float* buf, size_t count);
+bool mlp_tc_enabled(const g4_ctx* ctx);
+g4_status launch_decoder_feedforward_tc(g4_ctx* ctx, uint16_t* residual, const uint16_t* pre_w,
+                                        const uint8_t* up_p, const uint8_t* gate_p, const uint8_t* down_p,
+                                        const uint8_t* up_s, const uint8_t* gate_s, const uint8_t* down_s,
+                                        const float* up_gs, const float* gate_gs, const float* down_gs,
+                                        const uint16_t* post_w, const uint16_t* layer_scalar);
 
 // Raises `fn`'s dynamic shared-memory limit to the device's opt-in maximum, once per
 // (kernel, device): every launch, whatever its layout (`need` bytes, checked), then fits,

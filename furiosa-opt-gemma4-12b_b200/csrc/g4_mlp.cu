@@ -256,6 +256,9 @@ g4_status launch_decoder_feedforward(g4_ctx* ctx, uint16_t* residual, const uint
                                      const uint8_t* gate_s, const uint8_t* down_s, const float* up_gs,
                                      const float* gate_gs, const float* down_gs, const uint16_t* post_w,
                                      const uint16_t* layer_scalar) {
+  if (mlp_tc_enabled(ctx))
+    return launch_decoder_feedforward_tc(ctx, residual, pre_w, up_p, gate_p, down_p, up_s, gate_s, down_s, up_gs,
+                                         gate_gs, down_gs, post_w, layer_scalar);
   MlpOp op;
   op.residual = residual;
   op.pre_w = pre_w;

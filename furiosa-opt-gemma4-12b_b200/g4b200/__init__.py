@@ -68,6 +68,7 @@ LIB.g4_ctx_create.argtypes = [_i32, ctypes.POINTER(_vp)]
 LIB.g4_ctx_destroy.argtypes = [_vp]
 LIB.g4_ctx_set_stream.argtypes = [_vp, _vp]
 LIB.g4_ctx_set_wait_budget.argtypes = [_vp, _u32]
+LIB.g4_ctx_set_mlp_kernel.argtypes = [_vp, _i32]
 LIB.g4_ctx_poll_device_status.argtypes = [_vp, ctypes.POINTER(_u32)]
 LIB.g4_nccl_unique_id.argtypes = [ctypes.c_char_p]
 LIB.g4_ctx_init_tp.argtypes = [_vp, _i32, _i32, ctypes.c_char_p]
@@ -174,6 +175,13 @@ class Context:
         out = ctypes.c_int(0)
         self._check("g4_ctx_tp_peer_exchange", LIB.g4_ctx_tp_peer_exchange(self.handle, ctypes.byref(out)))
         return bool(out.value)
+
+    MLP_KERNELS = {"auto": 0, "stream": 1, "tensor": 2}
+
+    def set_mlp_kernel(self, kind: str) -> None:
+        """decoder_feedforward kernel of this context: "auto", "stream" (CUDA-core decode +
+        mma.sync) or "tensor" (tcgen05 block-scaled FP4; one GPU only)."""
+        self._check("g4_ctx_set_mlp_kernel", LIB.g4_ctx_set_mlp_kernel(self.handle, self.MLP_KERNELS[kind]))
 
     def set_wait_budget(self, timeout_us: int) -> None:
         self._check("g4_ctx_set_wait_budget", LIB.g4_ctx_set_wait_budget(self.handle, timeout_us))

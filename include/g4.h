@@ -110,6 +110,14 @@ const char* g4_ctx_last_error(const g4_ctx* ctx);
  * and cross-GPU waits inside fused kernels); default 2 s.  A wait that runs out sets a
  * bit in the context's device status word and its kernel returns early. */
 g4_status g4_ctx_set_wait_budget(g4_ctx* ctx, uint32_t timeout_us);
+/* Which kernel runs decoder_feedforward on this context (no reference counterpart):
+ * G4_MLP_AUTO (default: G4B200_MLP_KERNEL=stream|tc in the environment, else the
+ * streaming kernel), G4_MLP_STREAM (CUDA-core NVFP4 decode + mma.sync, every tensor-
+ * parallel size), G4_MLP_TENSOR (tcgen05 block-scaled FP4 MMA; one GPU only -- a
+ * tensor-parallel context keeps the streaming kernel).  Same results within f32
+ * rounding of the dot products. */
+enum { G4_MLP_AUTO = 0, G4_MLP_STREAM = 1, G4_MLP_TENSOR = 2 };
+g4_status g4_ctx_set_mlp_kernel(g4_ctx* ctx, int kind);
 /* Synchronise the context's stream, then read and clear the device status word
  * (0 = no kernel reported a timeout or an out-of-range device offset).  Returns
  * G4_ERR_TIMEOUT / G4_ERR_BAD_ARG when a bit was set. */

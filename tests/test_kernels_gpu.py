@@ -55,21 +55,57 @@ def _mlp_oracle(m: dict) -> np.ndarray:
         np.float32(a["down_global_scale"][0]), f(a["layer_scalar"])[0])
 
 
-def test_decoder_feedforward_baseline_config1(gpu_ctx):
+@pytest.fixture(params=["stream", "tensor"])
+def mlp_ctx(gpu_ctx, request):
+    """The shared context with one decoder_feedforward kernel selected."""
+    gpu_ctx.set_mlp_kernel(request.param)
+    yield gpu_ctx
+    gpu_ctx.set_mlp_kernel("auto")
+
+
+@pytest.mark.parametrize("seed", [0, 1])
+def test_decoder_feedforward_baseline_config1(mlp_ctx, seed):
     """x ~ N(0,1), norms ~ N(0,0.1), NVFP4 weights from N(0,0.02)."""
-    m = quant.mlp_config1(seed=0, device="cpu")
+    m = quant.mlp_config1(seed=seed, device="cpu")
     want = _mlp_oracle(m)
     d = {k: v.cuda() for k, v in m.items()}
-    g4.decoder_feedforward(gpu_ctx, **d)
+    g4.decoder_feedforward(mlp_ctx, **d)
     got = d["residual"].float().cpu().numpy()
     r = cases.compare(want, got, 0.02)
     print(r)
     assert r["max_abs"] <= 2e-2 and r["rel_l2"] <= 1e-2, r
-    assert gpu_ctx.poll() == 0
+    assert mlp_ctx.poll() == 0
 
 
-def test_decoder_feedforward_repeat_and_graph_replay(gpu_ctx):
+def test_decoder_feedforward_wide_activation_range(gpu_ctx):
+    """Activations spanning many octaves (and exact zeros) in the same 16-element blocks:
+    the tensor-core kernel's fixed-point activation pieces must still match the oracle."""
+    m = quant.mlp_config1(seed=3, device="cpu")
+    gen = torch.Generator().manual_seed(11)
+    scale = torch.pow(2.0, torch.randint(-12, 6, (3840,), generator=gen).float())
+    x = (torch.randn(3840, generator=gen) * scale)
+    x[torch.rand(3840, generator=gen) < 0.05] = 0.0
+    m["residual"] = x.to(torch.bfloat16)
+    want = _mlp_oracle(m)
+    outs = {}
+    for kind in ("stream", "tensor"):
+        gpu_ctx.set_mlp_kernel(kind)
+        d = {k: v.cuda() for k, v in m.items()}
+        g4.decoder_feedforward(gpu_ctx, **d)
+        outs[kind] = d["residual"].float().cpu().numpy()
+        assert gpu_ctx.poll() == 0
+    gpu_ctx.set_mlp_kernel("auto")
+    for kind, got in outs.items():
+        r = cases.compare(want, got, 0.02)
+        print(kind, r)
+        assert r["rel_l2"] <= 1e-2, (kind, r)
+
+
+@pytest.mark.parametrize("kind", ["stream", "tensor"])
+def test_decoder_feedforward_repeat_and_graph_replay(gpu_ctx, kind):
     import harness
+
+    gpu_ctx.set_mlp_kernel(kind)
 
     c = harness.build_case("decoder_feedforward")
     base = harness.mlp_tensors(c)
@@ -85,6 +121,7 @@ def test_decoder_feedforward_repeat_and_graph_replay(gpu_ctx):
     # capture in a CUDA graph on a side stream, replay twice
     s = torch.cuda.Stream()
     ctx = g4.Context(0, stream=s)
+    ctx.set_mlp_kernel(kind)
     res = base["residual"].clone()
     t = dict(base)
     t["residual"] = res
@@ -101,6 +138,7 @@ def test_decoder_feedforward_repeat_and_graph_replay(gpu_ctx):
         assert torch.equal(res, outs[0])
     del graph
     ctx.close()
+    gpu_ctx.set_mlp_kernel("auto")
 
 
 def _rand_bf16(gen, shape, std):

@@ -19,12 +19,19 @@ CASES = list(cases.BUILDERS)
 REL_L2 = 1e-2
 
 
-@pytest.mark.parametrize("name", CASES)
-def test_reference_case(gpu_ctx, golden, name):
+CASE_KERNELS = [(n, "auto") for n in CASES] + [("decoder_feedforward", "tensor")]
+
+
+@pytest.mark.parametrize("name,kernel", CASE_KERNELS)
+def test_reference_case(gpu_ctx, golden, name, kernel):
     import harness
 
     c = harness.build_case(name)
-    got = harness.RUNNERS[name](gpu_ctx, c)
+    gpu_ctx.set_mlp_kernel(kernel)  # decoder_feedforward also through the tensor-core kernel
+    try:
+        got = harness.RUNNERS[name](gpu_ctx, c)
+    finally:
+        gpu_ctx.set_mlp_kernel("auto")
     if name == "final_norm_and_logits":
         assert got["_lm_checksum"] == int(golden[f"{name}.check.lm_head_weight"][0])
     labels = [k[len(name) + 1:] for k in golden.files if k.startswith(name + ".expected")]
