@@ -58,15 +58,22 @@ def measured_peaks() -> tuple[float, str]:
     return 6650.0, "fallback"
 
 
-def profile_traffic() -> float | None:
-    """dram bytes per launch of the MLP kernel from the committed ncu summary."""
+def profile_traffic(kernel: str) -> float | None:
+    """DRAM bytes per launch of `kernel` from the committed ncu summary."""
     p = ROOT / "profiles" / "decoder_feedforward_traffic.json"
     if p.exists():
         try:
-            return float(json.loads(p.read_text())["dram_bytes_per_launch"])
+            return float(json.loads(p.read_text())["dram_bytes_per_launch_by_kernel"][kernel])
         except Exception:
             return None
     return None
+
+
+def mlp_kernel_name(choice: str, world: int) -> str:
+    """Kernel decoder_feedforward runs with this bench choice (the library's own rule)."""
+    if choice == "auto":
+        choice = "tensor" if os.environ.get("G4B200_MLP_KERNEL") == "tc" else "stream"
+    return "mlp_tc_kernel" if (choice == "tensor" and world == 1) else "mlp_kernel"
 
 
 class ClockSampler:
@@ -154,6 +161,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         dist.broadcast_object_list(nid, src=0)
         tpinfo = (rank, world, nid[0])
     ctx = g4.Context(local_rank, stream=stream, tp=tpinfo)
+    ctx.set_mlp_kernel(args.mlp_kernel)
+    kernel = mlp_kernel_name(args.mlp_kernel, world)
     layers = make_layers(dev, rank, world)
     residual = layers[0]["residual"].clone()
 
@@ -248,7 +257,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     peak, peak_kind = measured_peaks()
     achieved = algorithmic_bytes(world) / (kernel_ms * 1e-3) / 1e9
-    traffic = profile_traffic() if world == 1 else None
+    traffic = profile_traffic(kernel) if world == 1 else None
     line = {
         "metric": METRIC, "value": round(ms_per_step * 1000.0, 3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6),
@@ -258,6 +267,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                    "global_batch": 1, "seq_len": 1, "parallelism": f"tp{world}",
                    "layers_cycled": NLAYERS, "l2": f"inputs larger than L2 ({NLAYERS} layers x "
                    f"{WEIGHT_BYTES / 1e6:.1f} MB weights cycled per step)",
+                   "kernel": kernel,
                    "launch": "CUDA graph of one round (one launch per layer) replayed; consecutive launches "
                              "overlap via programmatic dependent launch" + (
                                  "" if world == 1 else
@@ -336,6 +346,8 @@ def main() -> None:
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--ref-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mlp-kernel", choices=["auto", "stream", "tensor"], default="auto",
+                    help="decoder_feedforward kernel: streaming (CUDA-core decode) or tcgen05 (one GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

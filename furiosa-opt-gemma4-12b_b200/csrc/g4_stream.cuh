@@ -442,6 +442,9 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
   }
 
   // -------------------------------------------------------------------- consumers
+  // The lane plan depends on the geometry alone: work it out while the previous kernel
+  // on the stream finishes (and, for later phases, while the grid barrier completes).
+  LanePlan pl = make_plan<Op::kFmt>(op.geom(0), warp, lane, true);
   // Everything below may read what the previous kernel on the stream wrote (activations,
   // residual, this context's scratch counters and buffers).
   pdl_wait();
@@ -474,6 +477,7 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
   };
   for (int ph = 0; ph < Op::kPhases; ++ph) {
     if (ph > 0) {
+      pl = make_plan<Op::kFmt>(op.geom(ph), warp, lane, true);
       if (!op.between_phases(sm, ph, deadline)) ok = false;
     }
     const UnitGeom g = op.geom(ph);
@@ -483,7 +487,6 @@ __device__ __forceinline__ void stream_body(const Op& op, const StreamLayout& la
     const int n = op.items(ph);
     const uint32_t count = (cta < n) ? static_cast<uint32_t>((n - cta + G - 1) / G) : 0u;
     const uint32_t first = done;
-    const LanePlan pl = make_plan<Op::kFmt>(g, warp, lane, true);
     // pseudo-row grp of A sits at (row grp, column col), of B at (row grp+8, column 4+col)
     const bool st_a = t == (pl.col >> 1), st_b = t == 2 + (pl.col >> 1), odd = (pl.col & 1) != 0;
     for (uint32_t m = 0; m < count; ++m) {
