@@ -193,6 +193,16 @@ __device__ __forceinline__ bool group_aborted(Smem& sm, int g);
 // ue4m3 code of 2^k, -9 <= k <= 0 (k >= -6 normal, below that subnormal)
 __device__ __forceinline__ uint32_t ue4m3_pow2(int k) { return k >= -6 ? static_cast<uint32_t>(k + 7) << 3 : 1u << (k + 9); }
 
+// w[b] = byte b of a, b, c, d (in that order, a's in the low byte)
+__device__ __forceinline__ void byte_transpose4(uint32_t a, uint32_t b, uint32_t c, uint32_t d, uint32_t (&w)[4]) {
+  const uint32_t abl = __byte_perm(a, b, 0x5140), abh = __byte_perm(a, b, 0x7362);
+  const uint32_t cdl = __byte_perm(c, d, 0x5140), cdh = __byte_perm(c, d, 0x7362);
+  w[0] = __byte_perm(abl, cdl, 0x5410);
+  w[1] = __byte_perm(abl, cdl, 0x7632);
+  w[2] = __byte_perm(abh, cdh, 0x5410);
+  w[3] = __byte_perm(abh, cdh, 0x7632);
+}
+
 // Writes one 16-element block of bf16 values (two per word, element 2i in the low half)
 // as kPieces NVFP4 pieces at local k-stage kl, block bs of the stage.
 //   Every element is aligned to the block's reference exponent eb as a 32-bit fixed-point
@@ -223,16 +233,21 @@ __device__ __forceinline__ void split_block(const uint32_t (&xw)[8], int gmax, S
     T[i] = (mv == 0u || off >= 32) ? 0u : (off <= 24 ? mv << (24 - off) : mv >> (off - 24));
   }
   sm.sblk[kl * 16 + bs] = static_cast<uint8_t>(ue4m3_pow2(eb - gmax));  // the same for all pieces
+  // Byte transpose: EA[b] = byte b of T of elements 0, 2, 4, 6 and OA[b] of elements
+  // 1, 3, 5, 7 (EB, OB: elements 8..15).  Piece n's digit sits at bit 6 - 2 (n % 4) of
+  // byte 3 - n / 4, so one shift and mask per operand puts element 2j's digit in nibble 2j
+  // and element 2j+1's in nibble 2j+1 of the piece's code word.
+  uint32_t EA[4], OA[4], EB[4], OB[4];
+  byte_transpose4(T[0], T[2], T[4], T[6], EA);
+  byte_transpose4(T[1], T[3], T[5], T[7], OA);
+  byte_transpose4(T[8], T[10], T[12], T[14], EB);
+  byte_transpose4(T[9], T[11], T[13], T[15], OB);
   uint8_t* codes = sm.bpc[kl];
 #pragma unroll
   for (int n = 0; n < kPieces; ++n) {
-    const int sh = 30 - 2 * n;
-    uint32_t lo = 0u, hi = 0u;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      lo |= ((T[i] >> sh) & 3u) << (4 * i);
-      hi |= ((T[i + 8] >> sh) & 3u) << (4 * i);
-    }
+    const int b = 3 - (n >> 2), sh = 6 - 2 * (n & 3);
+    const uint32_t lo = ((EA[b] >> sh) & 0x03030303u) | ((sh >= 4 ? OA[b] >> (sh - 4) : OA[b] << (4 - sh)) & 0x30303030u);
+    const uint32_t hi = ((EB[b] >> sh) & 0x03030303u) | ((sh >= 4 ? OB[b] >> (sh - 4) : OB[b] << (4 - sh)) & 0x30303030u);
     const uint32_t off = static_cast<uint32_t>(n) * 128u + ((static_cast<uint32_t>((bs >> 1) ^ (n & 7))) << 4) +
                          static_cast<uint32_t>(bs & 1) * 8u;
     *reinterpret_cast<uint2*>(codes + off) = make_uint2(lo | sgn_lo, hi | sgn_hi);
