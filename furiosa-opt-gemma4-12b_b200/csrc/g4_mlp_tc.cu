@@ -118,6 +118,9 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
+__device__ __forceinline__ void tc_commit_at(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
 __device__ __forceinline__ void tc_mma(uint32_t d, uint64_t da, uint64_t db, uint32_t sfa, uint32_t sfb, uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -486,8 +489,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      uint32_t k = 0, nseg = 0;
+      uint32_t k = 0, nseg = 0, slot = 0;  // slot = k % kStages
       bool ok = true;
+      // The issuer's per-stage work is a few adds: while it runs, the tensor pipe only has
+      // the MMAs already queued.  Descriptors hold address / 16 in their low 14 bits, so a
+      // ring slot (16 KB) is +1024 and a 64-k step (32 bytes) +2; a piece stage is +128.
+      const uint64_t desc_a0 = desc_sw128(smem_u32(sm.a[0])), desc_b0 = desc_sw128(smem_u32(sm.bpc[0]));
+      const uint32_t empty0 = smem_u32(&sm.empty[0]);
       for (int ph = 0; ph < 2 && ok; ++ph) {
         const Part& P = parts[ph];
         const int lo = P.lo(cta, G), hi = P.lo(cta + 1, G);
@@ -501,45 +509,45 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        const int s_a = lo % P.S;  // phase 1: first k-stage of the resident window
+        const int S = P.S, s_a = lo % S;  // phase 1: first k-stage of the resident window
         for (int si = 0; si < sm.seg_n[ph] && ok; ++si) {
-        const int k0 = sm.seg_k0[ph][si], k1 = sm.seg_k1[ph][si];
-        for (int ks = k0; ks < k1 && ok; ++ks, ++k) {
-          const bool first = ks == k0, last = ks == k1 - 1;
+          const int k0 = sm.seg_k0[ph][si], k1 = sm.seg_k1[ph][si];
           const uint32_t buf = nseg & 1u;
-          if (first && nseg >= 2) {
+          if (nseg >= 2) {
             if (!wait_bar(&sm.dempty[buf], ((nseg >> 1) - 1) & 1u, sm, status)) {
               ok = false;
               break;
             }
             tc_fence_after();
           }
-          const uint32_t slot = k % kStages;
-          // the scale warps waited for a stage's TMA barrier before arriving, so their
-          // barrier covers both the weights and their scales
-          if (k >= ready) {
-            const uint32_t j = min(k + kWaitGroup - 1u, k_end - 1u);
-            if (!wait_bar(&sm.sfready[j % kStages], (j / kStages) & 1u, sm, status)) {
-              ok = false;
-              break;
+          const uint32_t d = tbase + buf * 16u;
+          // resident k-stage of the activation pieces: ks itself when the whole phase is
+          // resident, else the position in this CTA's window (consecutive within a segment)
+          uint32_t kl = static_cast<uint32_t>(S <= kMaxLocal ? k0 : (k0 - s_a + S) % S);
+          for (int ks = k0; ks < k1; ++ks, ++k) {
+            // the scale warps waited for a stage's TMA barrier before arriving, so their
+            // barrier covers both the weights and their scales
+            if (k >= ready) {
+              const uint32_t j = min(k + kWaitGroup - 1u, k_end - 1u);
+              if (!wait_bar(&sm.sfready[j % kStages], (j / kStages) & 1u, sm, status)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              ready = j + 1u;
             }
-            tc_fence_after();
-            ready = j + 1u;
-          }
-          const int kl = (P.S <= kMaxLocal) ? ks : (ks - s_a + P.S) % P.S;
-          const uint32_t d = tbase + buf * 16u, t_sfa = tbase + kColSfa + 16u * slot,
-                         t_sfb = tbase + kColSfb + 16u * static_cast<uint32_t>(kl);
-          const uint32_t a0 = smem_u32(sm.a[slot]), b0 = smem_u32(sm.bpc[kl]);
+            const uint64_t da = desc_a0 + 1024u * slot, db = desc_b0 + 128u * kl;
+            const uint32_t t_sfa = tbase + kColSfa + 16u * slot, t_sfb = tbase + kColSfb + 16u * kl;
 #pragma unroll
-          for (int st = 0; st < 4; ++st)
-            tc_mma(d, desc_sw128(a0 + 32u * st), desc_sw128(b0 + 32u * st), t_sfa + 4u * st, t_sfb + 4u * st,
-                   (first && st == 0) ? 0u : 1u);
-          tc_commit(&sm.empty[slot]);
-          if (last) {
-            tc_commit(&sm.dfull[buf]);
-            ++nseg;
+            for (int st = 0; st < 4; ++st)
+              tc_mma(d, da + 2u * st, db + 2u * st, t_sfa + 4u * st, t_sfb + 4u * st, (ks == k0 && st == 0) ? 0u : 1u);
+            tc_commit_at(empty0 + 8u * slot);
+            slot = slot + 1u == static_cast<uint32_t>(kStages) ? 0u : slot + 1u;
+            ++kl;
           }
-        }
+          if (!ok) break;
+          tc_commit(&sm.dfull[buf]);
+          ++nseg;
         }
       }
       if (!ok) sm.abort_flag = 1;
