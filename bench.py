@@ -72,7 +72,7 @@ def profile_traffic(kernel: str) -> float | None:
 def mlp_kernel_name(choice: str, world: int) -> str:
     """Kernel decoder_feedforward runs with this bench choice (the library's own rule)."""
     if choice == "auto":
-        choice = "tensor" if os.environ.get("G4B200_MLP_KERNEL") == "tc" else "stream"
+        choice = "stream" if os.environ.get("G4B200_MLP_KERNEL") == "stream" else "tensor"
     return "mlp_tc_kernel" if (choice == "tensor" and world == 1) else "mlp_kernel"
 
 

@@ -854,14 +854,14 @@ static bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t c
 
 }  // namespace tc
 
-// Whether the tensor-core kernel serves this context: asked for (per context, else by
-// G4B200_MLP_KERNEL=tc) and one GPU (tensor-parallel shards use the streaming kernel and
-// its fused all-reduce).
+// Whether the tensor-core kernel serves this context: the default on one GPU, unless the
+// context asks for the streaming kernel (or G4B200_MLP_KERNEL=stream sets the default);
+// tensor-parallel shards use the streaming kernel and its fused all-reduce.
 bool mlp_tc_enabled(const g4_ctx* ctx) {
   static const int env_kind = [] {
     const char* e = std::getenv("G4B200_MLP_KERNEL");
-    if (e != nullptr && std::strcmp(e, "tc") == 0) return static_cast<int>(G4_MLP_TENSOR);
-    return static_cast<int>(G4_MLP_STREAM);
+    if (e != nullptr && std::strcmp(e, "stream") == 0) return static_cast<int>(G4_MLP_STREAM);
+    return static_cast<int>(G4_MLP_TENSOR);
   }();
   const int kind = ctx->mlp_kernel == G4_MLP_AUTO ? env_kind : ctx->mlp_kernel;
   return kind == G4_MLP_TENSOR && ctx->tp_world == 1 && ctx->buf.tc_seg != nullptr;

@@ -112,7 +112,7 @@ const char* g4_ctx_last_error(const g4_ctx* ctx);
 g4_status g4_ctx_set_wait_budget(g4_ctx* ctx, uint32_t timeout_us);
 /* Which kernel runs decoder_feedforward on this context (no reference counterpart):
  * G4_MLP_AUTO (default: G4B200_MLP_KERNEL=stream|tc in the environment, else the
- * streaming kernel), G4_MLP_STREAM (CUDA-core NVFP4 decode + mma.sync, every tensor-
+ * tcgen05 kernel on one GPU and the streaming kernel under tensor parallelism), G4_MLP_STREAM (CUDA-core NVFP4 decode + mma.sync, every tensor-
  * parallel size), G4_MLP_TENSOR (tcgen05 block-scaled FP4 MMA; one GPU only -- a
  * tensor-parallel context keeps the streaming kernel).  Same results within f32
  * rounding of the dot products. */

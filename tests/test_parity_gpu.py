@@ -19,7 +19,7 @@ CASES = list(cases.BUILDERS)
 REL_L2 = 1e-2
 
 
-CASE_KERNELS = [(n, "auto") for n in CASES] + [("decoder_feedforward", "tensor")]
+CASE_KERNELS = [(n, "auto") for n in CASES] + [("decoder_feedforward", "stream")]
 
 
 @pytest.mark.parametrize("name,kernel", CASE_KERNELS)
@@ -27,7 +27,7 @@ def test_reference_case(gpu_ctx, golden, name, kernel):
     import harness
 
     c = harness.build_case(name)
-    gpu_ctx.set_mlp_kernel(kernel)  # decoder_feedforward also through the tensor-core kernel
+    gpu_ctx.set_mlp_kernel(kernel)  # decoder_feedforward through both kernels ("auto" = tcgen05)
     try:
         got = harness.RUNNERS[name](gpu_ctx, c)
     finally:
