@@ -386,12 +386,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   pdl_launch_dependents();
   const uint32_t tbase = sm.tmem_base;
-  // The tail's operands that no CTA of this launch writes; each warp loads its share as
-  // its role ends (the residual was written by the previous kernel on the stream)
+  // The tail's operands that no CTA of this launch writes (the residual was written by the
+  // previous kernel on the stream).  The last CTA loads them together with the partial
+  // sums: one round trip, and no load in flight at the ticket or the teardown barrier.
   uint4 tail_rv = make_uint4(0u, 0u, 0u, 0u), tail_wv = tail_rv;
   float tail_gsd = 0.f, tail_ls = 0.f;
-  auto tail_prefetch = [&]() {
-    {  // every CTA may be the last one
+  auto tail_loads = [&]() {
+    {
       pdl_wait();
       if (tid < H / 8) {
         tail_rv = __ldcg(reinterpret_cast<const uint4*>(args.residual) + tid);
@@ -738,7 +739,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (epi && !ab1) run_epilogue(1);
     named_bar_sync(kBarGroup, kGroupThreads);
 
-    tail_prefetch();
     // ---- every CTA reports its partial sums; the last one to report adds the residual
     // branch (its ticket says every other CTA's sums are in: no waiting)
     if (g == 0) sm.last_flag = atom_add_acq_rel_gpu(&args.scr->mlp_done, 1u) == static_cast<uint32_t>(G - 1) ? 1 : 0;
@@ -746,15 +746,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ---- teardown: every tensor-core operation has completed (the epilogue consumed the
   // last accumulator, or the launch gave up).  The last CTA then adds the residual branch
-  // with all its warps: thread t < 480 owns outputs [8t, 8t + 8), so its partial-sum
-  // loads go out in one round (its residual and norm-weight loads were issued earlier).
-  if (warp < kGroupWarp0 || warp >= kSfWarp0) tail_prefetch();
+  // with all its warps: thread t < 480 owns outputs [8t, 8t + 8), so its partial-sum,
+  // residual and norm-weight loads go out in one round.
   tc_fence_before();
   __syncthreads();
   if (sm.last_flag && !aborted(sm)) {
     const int grp = tid;
     float y[8];
     float ss = 0.f;
+    tail_loads();
     if (grp < H / 8) {
       const int tile = (8 * grp) / 128, m0 = (8 * grp) % 128;
       const int first_owner = P1.owner(tile * P1.S, G);
