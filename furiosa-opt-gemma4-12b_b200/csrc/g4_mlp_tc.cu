@@ -196,6 +196,12 @@ __device__ __forceinline__ bool group_aborted(Smem& sm, int g);
 // ue4m3 code of 2^k, -9 <= k <= 0 (k >= -6 normal, below that subnormal)
 __device__ __forceinline__ uint32_t ue4m3_pow2(int k) { return k >= -6 ? static_cast<uint32_t>(k + 7) << 3 : 1u << (k + 9); }
 
+// x >> s with shifts of 32 or more giving 0 (the PTX shift clamps its amount)
+__device__ __forceinline__ uint32_t shr_clamped(uint32_t x, uint32_t s) {
+  uint32_t r;
+  asm("shr.b32 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(s));
+  return r;
+}
 // w[b] = byte b of a, b, c, d (in that order, a's in the low byte)
 __device__ __forceinline__ void byte_transpose4(uint32_t a, uint32_t b, uint32_t c, uint32_t d, uint32_t (&w)[4]) {
   const uint32_t abl = __byte_perm(a, b, 0x5140), abh = __byte_perm(a, b, 0x7362);
@@ -215,45 +221,55 @@ __device__ __forceinline__ void byte_transpose4(uint32_t a, uint32_t b, uint32_t
 //   largest; smaller ones are truncated there (below f32 rounding of the dot product).
 //   gmax >= every element's biased exponent; eb >= gmax - 9 keeps the block scale in range.
 __device__ __forceinline__ void split_block(const uint32_t (&xw)[8], int gmax, Smem& sm, int kl, int bs) {
-  uint32_t T[16], sgn_lo = 0u, sgn_hi = 0u;
-  int ex[16];
-  int eb = 0;
+  // exponent fields of both halves of each word (a zero exponent -- zero or subnormal --
+  // counts as 1, the subnormals' scale); eb = the block's largest, at least gmax - 9
+  uint32_t ew[8], emax2 = 0u;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const uint32_t u = (i & 1) ? (xw[i >> 1] >> 16) : (xw[i >> 1] & 0xFFFFu);
-    const uint32_t e = (u >> 7) & 0xFFu, mant = u & 0x7Fu;
-    T[i] = e ? (mant | 0x80u) : mant;  // significand M (subnormals: exponent 1, no hidden bit)
-    ex[i] = e ? static_cast<int>(e) : 1;
-    if (T[i]) eb = max(eb, ex[i]);
-    const uint32_t sbit = (u >> 15) << (4 * (i & 7) + 3);
-    if (i < 8) sgn_lo |= sbit; else sgn_hi |= sbit;
+  for (int i = 0; i < 8; ++i) {
+    ew[i] = (xw[i] >> 7) & 0x00FF00FFu;
+    emax2 = __vmaxu2(emax2, ew[i]);
   }
+  int eb = max(max(static_cast<int>(emax2 & 0xFFu), static_cast<int>(emax2 >> 16)), 1);
   eb = max(eb, gmax - 9);
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int off = eb - ex[i];
-    const uint32_t mv = T[i];
-    T[i] = (mv == 0u || off >= 32) ? 0u : (off <= 24 ? mv << (24 - off) : mv >> (off - 24));
-  }
   sm.sblk[kl * 16 + bs] = static_cast<uint8_t>(ue4m3_pow2(eb - gmax));  // the same for all pieces
+  // T = significand in the top byte, shifted right by eb - e (shifts of 32 or more give 0);
+  // the sign of element i goes to bit 4 (i % 8) + 3 of its half's code words
+  uint32_t T[16], sgn_lo = 0u, sgn_hi = 0u;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t sig = (xw[i] & 0x007F007Fu) | (__vsetne2(ew[i], 0u) << 7);
+    const int e0 = max(static_cast<int>(ew[i] & 0xFFu), 1), e1 = max(static_cast<int>(ew[i] >> 16), 1);
+    T[2 * i] = shr_clamped(__byte_perm(sig, 0u, 0x0444), static_cast<uint32_t>(eb - e0));
+    T[2 * i + 1] = shr_clamped(__byte_perm(sig, 0u, 0x2444), static_cast<uint32_t>(eb - e1));
+    const uint32_t sg = ((xw[i] >> 12) & 0x8u) | ((xw[i] >> 24) & 0x80u);
+    if (i < 4) sgn_lo |= sg << (8 * i); else sgn_hi |= sg << (8 * (i - 4));
+  }
   // Byte transpose: EA[b] = byte b of T of elements 0, 2, 4, 6 and OA[b] of elements
-  // 1, 3, 5, 7 (EB, OB: elements 8..15).  Piece n's digit sits at bit 6 - 2 (n % 4) of
-  // byte 3 - n / 4, so one shift and mask per operand puts element 2j's digit in nibble 2j
-  // and element 2j+1's in nibble 2j+1 of the piece's code word.
+  // 1, 3, 5, 7 (EB, OB: elements 8..15).  Z interleaves them per byte: low nibble from the
+  // even element, high nibble from the odd one, so the digit at bits 2p, 2p+1 of byte b of
+  // T (piece 15 - 4b - p) of both elements is one shift and mask away; the code word of
+  // piece n has element 2j's digit in nibble 2j and element 2j+1's in nibble 2j+1.
   uint32_t EA[4], OA[4], EB[4], OB[4];
   byte_transpose4(T[0], T[2], T[4], T[6], EA);
   byte_transpose4(T[1], T[3], T[5], T[7], OA);
   byte_transpose4(T[8], T[10], T[12], T[14], EB);
   byte_transpose4(T[9], T[11], T[13], T[15], OB);
   uint8_t* codes = sm.bpc[kl];
+  const uint32_t half = static_cast<uint32_t>(bs & 1) * 8u, chunk = static_cast<uint32_t>(bs >> 1);
 #pragma unroll
-  for (int n = 0; n < kPieces; ++n) {
-    const int b = 3 - (n >> 2), sh = 6 - 2 * (n & 3);
-    const uint32_t lo = ((EA[b] >> sh) & 0x03030303u) | ((sh >= 4 ? OA[b] >> (sh - 4) : OA[b] << (4 - sh)) & 0x30303030u);
-    const uint32_t hi = ((EB[b] >> sh) & 0x03030303u) | ((sh >= 4 ? OB[b] >> (sh - 4) : OB[b] << (4 - sh)) & 0x30303030u);
-    const uint32_t off = static_cast<uint32_t>(n) * 128u + ((static_cast<uint32_t>((bs >> 1) ^ (n & 7))) << 4) +
-                         static_cast<uint32_t>(bs & 1) * 8u;
-    *reinterpret_cast<uint2*>(codes + off) = make_uint2(lo | sgn_lo, hi | sgn_hi);
+  for (int b = 0; b < 4; ++b) {
+    const uint32_t zl0 = (EA[b] & 0x0F0F0F0Fu) | ((OA[b] << 4) & 0xF0F0F0F0u);
+    const uint32_t zh0 = ((EA[b] >> 4) & 0x0F0F0F0Fu) | (OA[b] & 0xF0F0F0F0u);
+    const uint32_t zl1 = (EB[b] & 0x0F0F0F0Fu) | ((OB[b] << 4) & 0xF0F0F0F0u);
+    const uint32_t zh1 = ((EB[b] >> 4) & 0x0F0F0F0Fu) | (OB[b] & 0xF0F0F0F0u);
+    const uint32_t words[4][2] = {{zl0, zl1}, {zl0 >> 2, zl1 >> 2}, {zh0, zh1}, {zh0 >> 2, zh1 >> 2}};
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const uint32_t n = static_cast<uint32_t>(15 - 4 * b - p);
+      const uint32_t off = n * 128u + ((chunk ^ (n & 7u)) << 4) + half;
+      *reinterpret_cast<uint2*>(codes + off) =
+          make_uint2((words[p][0] & 0x33333333u) | sgn_lo, (words[p][1] & 0x33333333u) | sgn_hi);
+    }
   }
 }
 
