@@ -262,8 +262,10 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   if (st == G4_OK) st = check_cuda(ctx, cudaMalloc(&b.ybuf, 3840 * 4), "cudaMalloc ybuf");
   if (st == G4_OK) st = check_cuda(ctx, cudaMalloc(&b.attn, kAttnFloats * 4), "cudaMalloc attn");
   if (st == G4_OK) st = check_cuda(ctx, cudaMalloc(&b.tc_seg, kTcSegFloats * 4), "cudaMalloc tc_seg");
-  if (st == G4_OK) st = check_cuda(ctx, cudaMalloc(&b.tc_cnt, kTcTiles * 4), "cudaMalloc tc_cnt");
-  if (st == G4_OK) st = check_cuda(ctx, cudaMemset(b.tc_cnt, 0, kTcTiles * 4), "cudaMemset tc_cnt");
+  if (st == G4_OK) st = check_cuda(ctx, cudaMalloc(&b.tc_ptag, kTcPartWords * 8), "cudaMalloc tc_ptag");
+  if (st == G4_OK) st = check_cuda(ctx, cudaMemset(b.tc_ptag, 0, kTcPartWords * 8), "cudaMemset tc_ptag");
+  if (st == G4_OK) st = check_cuda(ctx, cudaMalloc(&b.tc_htag, kHFloats * 4), "cudaMalloc tc_htag");
+  if (st == G4_OK) st = check_cuda(ctx, cudaMemset(b.tc_htag, 0, kHFloats * 4), "cudaMemset tc_htag");
   if (st == G4_OK) st = check_cuda(ctx, cudaDeviceSynchronize(), "ctx init");
   if (st != G4_OK) {
     g4_ctx_destroy(ctx);
@@ -286,7 +288,8 @@ g4_status g4_ctx_destroy(g4_ctx* ctx) {
   cudaFree(ctx->buf.attn);
   cudaFree(ctx->buf.xch);
   cudaFree(ctx->buf.tc_seg);
-  cudaFree(ctx->buf.tc_cnt);
+  cudaFree(ctx->buf.tc_ptag);
+  cudaFree(ctx->buf.tc_htag);
   delete ctx;
   return G4_OK;
 }

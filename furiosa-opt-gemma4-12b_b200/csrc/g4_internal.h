@@ -23,7 +23,7 @@ struct Scratch {
   uint32_t proj_done;         // o-proj: CTAs done
   uint32_t lm_done;           // (reserved)
   uint32_t xch_epoch;         // TP: launches that used the peer exchange (same on every rank)
-  uint32_t pad0;
+  uint32_t tc_epoch;          // tensor-core MLP: launches finished (tags the values CTAs exchange)
   uint32_t head_count[64];    // qkv: completed items per head group
   uint32_t attn_count[64];    // split-KV attention: completed chunks per kv head
   uint32_t attn_done;         // paged attention: CTAs done
@@ -36,6 +36,7 @@ constexpr size_t kHFloats = 15360;                // MLP intermediate (bf16 stor
 constexpr size_t kAttnFloats = 512 * (2 * 16 + 16 * 512) + 4096;  // 512 chunks of 16 heads
 constexpr size_t kTcTiles = 15360 / 64 + 3840 / 128;              // gate/up tiles + down tiles
 constexpr size_t kTcSegFloats = kTcTiles * 8 * 128;               // 8 segment slots of 128 rows
+constexpr size_t kTcPartWords = (15360 / 64) * 8 * 128;           // tagged gate/up segment partials
 
 // Tensor-parallel one-shot all-reduce over peer memory.  Each rank owns one exchange
 // buffer of 64-bit words, word[2][kMaxTp][3840]: two halves used by alternate launches,
@@ -63,7 +64,10 @@ struct DeviceBuffers {
   float* attn = nullptr;     // [kAttnFloats] split-KV partials
   uint64_t* xch = nullptr;   // [kXchWords] TP peer exchange (this rank's, IPC-exported)
   float* tc_seg = nullptr;   // [kTcSegFloats] tensor-core MLP: per-tile segment partials
-  uint32_t* tc_cnt = nullptr;  // [kTcTiles] tensor-core MLP: segments finished per tile (zero between launches)
+  // Tensor-core MLP values exchanged between CTAs, each word tagged with the launch that
+  // wrote it (zero at creation): gate/up segment partials {f32, tag} and h {bf16, tag}.
+  uint64_t* tc_ptag = nullptr;  // [kTcPartWords]
+  uint32_t* tc_htag = nullptr;  // [kHFloats]
 };
 
 }  // namespace g4

@@ -17,10 +17,12 @@
 // pairs are cut into 148 contiguous ranges (stream-K): CTA c owns pairs
 // [c*W/G, (c+1)*W/G).  A CTA's run inside one tile is a segment; its MMAs accumulate in
 // one of two TMEM accumulators.  Phase 0 finishes a tile (GeGLU -> h) in the CTA holding
-// its first k-stages, adding the other part's partial sums (k order) once its count says
-// they are in; phase 1 leaves every segment's 128 partial sums in a per-tile slot and
-// the tail adds them in k order.  A grid barrier separates the phases; the last CTA to
-// finish runs the RMSNorm/residual tail.
+// its first k-stages, adding the other parts' partial sums (k order); phase 1 leaves every
+// segment's 128 partial sums in a per-tile slot and the last CTA to finish adds them in k
+// order and runs the RMSNorm/residual tail.  Values one CTA hands to another inside a
+// launch (gate/up partial sums, h) are words tagged with the launch's number: a reader
+// re-reads a word until its tag is current, so neither a flag nor a grid barrier stands
+// between the phases, and a value already written costs one round trip.
 //
 // Warps: 0 TMA producer, 1 TMEM owner + MMA issuer, 12-15 write each stage's weight
 // scales into tensor memory (tcgen05.st, one lane quarter each: the tensor pipe only runs
@@ -78,6 +80,7 @@ struct __align__(1024) Smem {
   int abort_flag;     // some wait gave up (any warp may set it)
   int grp_abort;      // snapshot of abort_flag taken before a staging-group barrier
   int last_flag;
+  uint32_t tag;       // this launch's tag (launches finished + 1) for the words CTAs exchange
   float gate_gs, up_gs;
 };
 
@@ -91,9 +94,9 @@ struct Args {
   const float* down_gs;
   Scratch* scr;
   float* part;       // [H] down-projection sums
-  uint16_t* hbuf;    // [L] h (bf16)
-  float* seg;        // [(T0 + T1) * kMaxSeg * 128] segment partials
-  uint32_t* cnt;     // [T0 + T1] segments finished per tile
+  float* seg;        // [(T0 + T1) * kMaxSeg * 128] segment partials (down phase)
+  uint64_t* ptag;    // [T0 * kMaxSeg * 128] gate/up segment partials {f32 bits, launch tag}
+  uint32_t* htag;    // [L] h {bf16 bits, launch tag in the high half}
   int lrows;         // intermediate rows
   uint64_t budget_ns;
 };
@@ -607,6 +610,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (g == 0) {
         sm.gate_gs = __ldg(args.gate_gs);
         sm.up_gs = __ldg(args.up_gs);
+        sm.tag = __ldcg(&args.scr->tc_epoch) + 1u;  // the previous launch's count (after the wait)
       }
       if (g < nblk) {
         const uint32_t xw[8] = {xv[0].x, xv[0].y, xv[0].z, xv[0].w, xv[1].x, xv[1].y, xv[1].z, xv[1].w};
@@ -646,16 +650,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float g2 = round_bf16(round_bf16(tot) * sm.gate_gs);
         const float u2 = round_bf16(round_bf16(sm.xchg[m]) * sm.up_gs);
         hv = round_bf16(round_bf16(gelu_tanh(g2)) * u2);
-        args.hbuf[tile * 64 + m] = f32_to_bf16(hv);
+        st_relaxed_gpu_u32(&args.htag[tile * 64 + m], static_cast<uint32_t>(f32_to_bf16(hv)) | (sm.tag << 16));
       }
-      const float mx = warp_max(fabsf(hv));
-      if (lane == 0 && m < 64) atomicMax(&args.scr->mlp_amax, __float_as_uint(mx));
     };
     // Accumulator epilogue of one phase (warps 4..7), segments in the MMA order.  Phase 0:
-    // a whole tile is finished here; a split tile's tail part stores its partial sums and
-    // bumps the tile's count (release); the head part's CTA owns the tile: it waits for
-    // the count, adds the parts in k order and finishes the tile.  Phase 1: partial sums
-    // only (the tail adds them).
+    // a whole tile is finished here; a split tile's tail part stores its partial sums as
+    // tagged words; the head part's CTA owns the tile: it reads the other parts' words
+    // (again until their tags are this launch's: one round trip when they are in), adds
+    // the parts in k order and finishes the tile.  Phase 1: partial sums only (the tail
+    // adds them).
     auto run_epilogue = [&](int ph) {
       const Part& P = parts[ph];
       const int tbase_idx = (ph == 0) ? 0 : P0.T;
@@ -679,33 +682,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&sm.dempty[buf]);
         ++nseg;
         float* slots = args.seg + static_cast<size_t>(tbase_idx + tile) * kMaxSeg * 128;
-        if (ph == 1 || segi > 0) {
+        uint64_t* tagged = args.ptag + static_cast<size_t>(tile) * kMaxSeg * 128 + m;
+        if (ph == 1) {
           slots[segi * 128 + m] = v;
-          if (ph == 0) {
-            named_bar_sync(kBarEpi, 128);
-            if (m == 0) red_add_release_gpu(&args.cnt[tile], 1u);
-          }
+        } else if (segi > 0) {
+          st_relaxed_gpu_u64(tagged + segi * 128, (static_cast<uint64_t>(sm.tag) << 32) | __float_as_uint(v));
         } else if (nseg_tile == 1) {
           geglu_store(tile, v);
         } else {
-          if (m == 0) {
-            uint32_t spins = 0;
-            int fail = 0;
-            while (ld_acquire_gpu(&args.cnt[tile]) < static_cast<uint32_t>(nseg_tile - 1)) {
-              if ((++spins & 63u) == 0u && global_ns() > sm.deadline) {
-                fail = 1;
-                break;
+          uint64_t w[kMaxSeg];
+          for (uint32_t round = 0;; ++round) {  // every part's word re-read each round
+            bool all = true;
+#pragma unroll
+            for (int sgi = 1; sgi < kMaxSeg; ++sgi)
+              if (sgi < nseg_tile) {
+                w[sgi] = ld_relaxed_gpu_u64(tagged + sgi * 128);
+                all = all && static_cast<uint32_t>(w[sgi] >> 32) == sm.tag;
               }
-            }
-            if (fail) {
+            if (all) break;
+            if ((round & 7u) == 7u && global_ns() > sm.deadline) {
               atomicOr(status, DEV_ERR_TIMEOUT_GRID);
               sm.abort_flag = 1;
+              break;
             }
-            args.cnt[tile] = 0u;  // every part has arrived: ready for the next launch
+            __nanosleep(128);
           }
-          named_bar_sync(kBarEpi, 128);
           float tot = v;
-          for (int sgi = 1; sgi < nseg_tile; ++sgi) tot += __ldcg(slots + sgi * 128 + m);
+#pragma unroll
+          for (int sgi = 1; sgi < kMaxSeg; ++sgi)  // the parts in k order
+            if (sgi < nseg_tile) tot += __uint_as_float(static_cast<uint32_t>(w[sgi]));
           geglu_store(tile, tot);
         }
         named_bar_sync(kBarEpi, 128);
@@ -714,35 +719,52 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (epi) run_epilogue(0);
     named_bar_sync(kBarGroup, kGroupThreads);
-    // ---- grid barrier: every CTA's h rows (and max |h|) are visible
-    if (g == 0) {
-      red_add_release_gpu(&args.scr->mlp_sync, 1u);
-      uint32_t spins = 0;
-      while (ld_acquire_gpu(&args.scr->mlp_sync) < static_cast<uint32_t>(G)) {
-        if ((++spins & 63u) == 0u && global_ns() > sm.deadline) {
-          atomicOr(status, DEV_ERR_TIMEOUT_GRID);
-          sm.abort_flag = 1;
-          break;
-        }
-      }
-    }
     // ---- phase 1 staging: pieces of h over this CTA's window of k-stages
     const bool ab1 = group_aborted(sm, g);
     if (!ab1) {
       const int lo = P1.lo(cta, G), hi = P1.lo(cta + 1, G);
       const int s_a = lo % P1.S;
       const int len = min(hi - lo, P1.S);
-      // largest biased exponent of h (max |h| gathered with atomicMax on its f32 bits)
-      const int gmax = static_cast<int>((__ldcg(&args.scr->mlp_amax) >> 23) & 0xFFu);
-      if (g < kPieces) sm.pw[1][g] = pow2f(gmax - 127 - 2 * g);
-      for (int wb = g; wb < len * 16; wb += kGroupThreads) {
-        const int kl = wb >> 4, bs = wb & 15;
+      // One 16-element block of h per thread (len * 16 <= 256 < 320), read as tagged
+      // words until every tag is this launch's: no grid barrier, and the words of tiles
+      // already finished arrive in one round trip.  The pieces' reference exponent is the
+      // largest of this CTA's window (each CTA scales its own partial sums).
+      const int kl = g >> 4, bs = g & 15;
+      const bool mine = g < len * 16;
+      uint32_t hw[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+      uint32_t hmax = 0u;
+      if (mine) {
         const int kstage = (s_a + kl) % P1.S;
-        const uint4* src = reinterpret_cast<const uint4*>(args.hbuf + kstage * kKStage + bs * 16);
-        const uint4 h0 = __ldcg(src), h1 = __ldcg(src + 1);
-        const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-        split_block(hw, gmax, sm, kl, bs);
+        const uint32_t* src = args.htag + kstage * kKStage + bs * 16;
+        const uint32_t tag16 = sm.tag & 0xFFFFu;
+        uint32_t t[16];
+        for (uint32_t round = 0;; ++round) {  // every word re-read each round: one round trip
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint4 v4 = ld_relaxed_gpu_v4u32(src + 4 * q);
+            t[4 * q] = v4.x, t[4 * q + 1] = v4.y, t[4 * q + 2] = v4.z, t[4 * q + 3] = v4.w;
+          }
+          bool all = true;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) all = all && (t[i] >> 16) == tag16;
+          if (all) break;
+          if ((round & 7u) == 7u && global_ns() > sm.deadline) {
+            atomicOr(status, DEV_ERR_TIMEOUT_GRID);
+            sm.abort_flag = 1;
+            break;
+          }
+          __nanosleep(128);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          hw[j] = (t[2 * j] & 0xFFFFu) | (t[2 * j + 1] << 16);
+          hmax = max(hmax, max(t[2 * j] & 0x7FFFu, t[2 * j + 1] & 0x7FFFu));
+        }
       }
+      const float2 rm = group_sum_max(0.f, __uint_as_float(hmax << 16), sm, g);
+      const int gmax = static_cast<int>((__float_as_uint(rm.y) >> 23) & 0xFFu);
+      if (g < kPieces) sm.pw[1][g] = pow2f(gmax - 127 - 2 * g);
+      if (mine) split_block(hw, gmax, sm, kl, bs);
     }
     fence_proxy_async();
     named_bar_sync(kBarGroup, kGroupThreads);
@@ -823,11 +845,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       *reinterpret_cast<uint4*>(args.residual + 8 * grp) = make_uint4(o[0], o[1], o[2], o[3]);
     }
-    if (tid == 0) {
-      args.scr->mlp_sync = 0u;
-      args.scr->mlp_amax = 0u;
-      args.scr->mlp_done = 0u;
-    }
+  }
+  if (sm.last_flag && tid == 0) {  // every CTA has read this launch's tag and taken a ticket
+    args.scr->mlp_done = 0u;
+    args.scr->tc_epoch = sm.tag;
   }
   if (warp == 1) {
     __syncwarp();
@@ -880,7 +901,8 @@ bool mlp_tc_enabled(const g4_ctx* ctx) {
     return static_cast<int>(G4_MLP_TENSOR);
   }();
   const int kind = ctx->mlp_kernel == G4_MLP_AUTO ? env_kind : ctx->mlp_kernel;
-  return kind == G4_MLP_TENSOR && ctx->tp_world == 1 && ctx->buf.tc_seg != nullptr;
+  return kind == G4_MLP_TENSOR && ctx->tp_world == 1 && ctx->buf.tc_seg != nullptr && ctx->buf.tc_ptag != nullptr &&
+         ctx->buf.tc_htag != nullptr;
 }
 
 g4_status launch_decoder_feedforward_tc(g4_ctx* ctx, uint16_t* residual, const uint16_t* pre_w, const uint8_t* up_p,
@@ -922,9 +944,9 @@ g4_status launch_decoder_feedforward_tc(g4_ctx* ctx, uint16_t* residual, const u
   a.down_gs = down_gs;
   a.scr = ctx->buf.scratch;
   a.part = ctx->buf.part;
-  a.hbuf = ctx->buf.hbuf;
   a.seg = ctx->buf.tc_seg;
-  a.cnt = ctx->buf.tc_cnt;
+  a.ptag = ctx->buf.tc_ptag;
+  a.htag = ctx->buf.tc_htag;
   a.lrows = lrows;
   a.budget_ns = ctx->wait_budget_ns;
   const size_t smem = sizeof(Smem) + 1024;
@@ -932,7 +954,7 @@ g4_status launch_decoder_feedforward_tc(g4_ctx* ctx, uint16_t* residual, const u
   if (st != G4_OK) return st;
   void* args[] = {&maps[0], &maps[1], &maps[2], &maps[3], &maps[4], &maps[5], &a};
   // Not cooperative (see launch_decoder_feedforward): one CTA per SM, and its shared memory
-  // excludes a second CTA, so the grid barrier sees every CTA resident.
+  // excludes a second CTA, so every CTA is resident while others wait for its words.
   return launch_kernel(ctx, (const void*)mlp_tc_kernel, dim3(G), dim3(kThreads), smem, args, false,
                        "launch mlp_tc_kernel");
 }
