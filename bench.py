@@ -70,11 +70,13 @@ def profile_traffic(kernel: str) -> float | None:
     return None
 
 
-def mlp_kernel_name(choice: str, world: int) -> str:
-    """Kernel decoder_feedforward runs with this bench choice (the library's own rule)."""
+def mlp_kernel_name(choice: str, world: int, peer: bool = False) -> str:
+    """Kernel decoder_feedforward runs with this bench choice (the library's own rule:
+    the tcgen05 kernel on one GPU, the streaming kernel under tensor parallelism)."""
     if choice == "auto":
         choice = "stream" if os.environ.get("G4B200_MLP_KERNEL") == "stream" else "tensor"
-    return "mlp_tc_kernel" if (choice == "tensor" and world == 1) else "mlp_kernel"
+    tc = choice == "tensor" and world == 1
+    return "mlp_tc_kernel" if tc else "mlp_kernel"
 
 
 class ClockSampler:
@@ -163,7 +165,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         tpinfo = (rank, world, nid[0])
     ctx = g4.Context(local_rank, stream=stream, tp=tpinfo)
     ctx.set_mlp_kernel(args.mlp_kernel)
-    kernel = mlp_kernel_name(args.mlp_kernel, world)
+    kernel = mlp_kernel_name(args.mlp_kernel, world, world > 1 and ctx.tp_peer_exchange)
     layers = make_layers(dev, rank, world)
     residual = layers[0]["residual"].clone()
 

@@ -81,6 +81,8 @@ struct __align__(1024) Smem {
   int grp_abort;      // snapshot of abort_flag taken before a staging-group barrier
   int last_flag;
   uint32_t tag;       // this launch's tag (launches finished + 1) for the words CTAs exchange
+  uint32_t xch_tag;   // tensor parallel: this launch's tag in the peer exchange
+  int xch_failed;
   float gate_gs, up_gs;
 };
 
@@ -97,8 +99,9 @@ struct Args {
   float* seg;        // [(T0 + T1) * kMaxSeg * 128] segment partials (down phase)
   uint64_t* ptag;    // [T0 * kMaxSeg * 128] gate/up segment partials {f32 bits, launch tag}
   uint32_t* htag;    // [L] h {bf16 bits, launch tag in the high half}
-  int lrows;         // intermediate rows
+  int lrows;         // intermediate rows of this rank's shard
   uint64_t budget_ns;
+  PeerXch xch;       // tensor parallel: every rank's exchange buffer (world <= 1: one GPU)
 };
 
 // ---------------------------------------------------------------- PTX wrappers
@@ -274,6 +277,65 @@ __device__ __forceinline__ void split_block(const uint32_t (&xw)[8], int gmax, S
           make_uint2((words[p][0] & 0x33333333u) | sgn_lo, (words[p][1] & 0x33333333u) | sgn_hi);
     }
   }
+}
+
+// Tensor-parallel sum of the down projection over NVLink peer memory, by the last CTA of
+// every rank (512 threads; thread t < 480 holds outputs [8t, 8t + 8)): the same one-shot
+// protocol as the streaming kernels' exchange.  Each value goes to every rank's buffer as
+// one 64-bit word {f32, launch tag} with a relaxed system-scope store; a rank re-reads its
+// own buffer until every rank's words carry this launch's tag and adds them in rank
+// order, so the ranks' results are bit-identical.  The halves of the buffer alternate
+// with the tag, so a rank one launch ahead never overwrites words a peer still reads.
+// The wait is bounded (DEV_ERR_TIMEOUT_PEER).
+__device__ __forceinline__ bool peer_allreduce_tc(const PeerXch& x, uint32_t* launch_ctr, float (&y)[8], int tid,
+                                                  uint32_t* status, Smem& sm) {
+  if (tid == 0) {
+    sm.xch_tag = *launch_ctr + 1u;
+    sm.xch_failed = 0;
+  }
+  __syncthreads();
+  const uint32_t e = sm.xch_tag;
+  if (tid < H / 8) {
+    const size_t half = static_cast<size_t>(e & 1u) * kMaxTp * H;
+    uint64_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w[i] = (static_cast<uint64_t>(e) << 32) | __float_as_uint(y[i]);
+    for (int p = 0; p < x.world; ++p) {
+      uint64_t* dst = x.buf[p] + half + static_cast<size_t>(x.rank) * H + 8 * tid;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) st_relaxed_sys_v2u64(dst + 2 * j, w[2 * j], w[2 * j + 1]);
+    }
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    bool ok = true;
+    for (int q = 0; q < x.world && ok; ++q) {
+      const uint64_t* src = x.buf[x.rank] + half + static_cast<size_t>(q) * H + 8 * tid;
+      uint64_t v[8];
+      for (uint32_t spins = 0;; ++spins) {
+        bool all = true;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          ld_relaxed_sys_v2u64(src + 2 * j, v[2 * j], v[2 * j + 1]);
+          all = all && static_cast<uint32_t>(v[2 * j] >> 32) == e && static_cast<uint32_t>(v[2 * j + 1] >> 32) == e;
+        }
+        if (all) break;
+        if ((spins & 255u) == 255u && global_ns() > sm.deadline) {
+          ok = false;
+          break;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += __uint_as_float(static_cast<uint32_t>(v[i]));
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = acc[i];
+    if (!ok) {
+      sm.xch_failed = 1;
+      atomicOr(status, DEV_ERR_TIMEOUT_PEER);
+    }
+  }
+  __syncthreads();
+  if (tid == 0) *launch_ctr = e;
+  return sm.xch_failed == 0;
 }
 
 // Stage partition of phase p: W = T*S (tile, k-stage) pairs over G CTAs.
@@ -722,9 +784,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- phase 1 staging: pieces of h over this CTA's window of k-stages
     const bool ab1 = group_aborted(sm, g);
     if (!ab1) {
+      // the whole down phase is resident when it fits (tensor-parallel shards), else this
+      // CTA's window of k-stages
+      const bool whole = P1.S <= kMaxLocal;
       const int lo = P1.lo(cta, G), hi = P1.lo(cta + 1, G);
-      const int s_a = lo % P1.S;
-      const int len = min(hi - lo, P1.S);
+      const int s_a = whole ? 0 : lo % P1.S;
+      const int len = whole ? P1.S : min(hi - lo, P1.S);
       // One 16-element block of h per thread (len * 16 <= 256 < 320), read as tagged
       // words until every tag is this launch's: no grid barrier, and the words of tiles
       // already finished arrive in one round trip.  The pieces' reference exponent is the
@@ -769,7 +834,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_proxy_async();
     named_bar_sync(kBarGroup, kGroupThreads);
     if (epi && !ab1) {
-      write_sfb(sm, tbase, min(P1.lo(cta + 1, G) - P1.lo(cta, G), P1.S) * 4, warp - kEpiWarp0);
+      write_sfb(sm, tbase, (P1.S <= kMaxLocal ? P1.S : min(P1.lo(cta + 1, G) - P1.lo(cta, G), P1.S)) * 4,
+                warp - kEpiWarp0);
       tc_fence_before();
     }
     named_bar_sync(kBarGroup, kGroupThreads);
@@ -791,7 +857,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (sm.last_flag && !aborted(sm)) {
     const int grp = tid;
     float y[8];
-    float ss = 0.f;
+    float t[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     tail_loads();
     if (grp < H / 8) {
       const int tile = (8 * grp) / 128, m0 = (8 * grp) % 128;
@@ -805,13 +871,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           pv[sgi][0] = __ldcg(sp + sgi * 32);
           pv[sgi][1] = __ldcg(sp + sgi * 32 + 1);
         }
-      float t[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int sgi = 0; sgi < kMaxSeg; ++sgi)  // the tile's segments in k order
         if (sgi < ns) {
           t[0] += pv[sgi][0].x, t[1] += pv[sgi][0].y, t[2] += pv[sgi][0].z, t[3] += pv[sgi][0].w;
           t[4] += pv[sgi][1].x, t[5] += pv[sgi][1].y, t[6] += pv[sgi][1].z, t[7] += pv[sgi][1].w;
         }
+    }
+    // tensor parallel: every rank's down sums, added in rank order on every rank
+    const bool xch_ok = args.xch.world <= 1 || peer_allreduce_tc(args.xch, &args.scr->xch_epoch, t, tid, status, sm);
+    float ss = 0.f;
+    if (grp < H / 8) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float d2 = round_bf16(round_bf16(t[i]) * tail_gsd);
@@ -826,7 +896,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int w = 0; w < kThreads / 32; ++w) tot += sm.red[w];
     const float rr = rms_factor(tot, H);
-    if (grp < H / 8) {
+    if (grp < H / 8 && xch_ok) {
       const uint32_t rw[4] = {tail_rv.x, tail_rv.y, tail_rv.z, tail_rv.w};
       const uint32_t ww[4] = {tail_wv.x, tail_wv.y, tail_wv.z, tail_wv.w};
       uint32_t o[4];
@@ -891,9 +961,13 @@ static bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t c
 
 }  // namespace tc
 
-// Whether the tensor-core kernel serves this context: the default on one GPU, unless the
-// context asks for the streaming kernel (or G4B200_MLP_KERNEL=stream sets the default);
-// tensor-parallel shards use the streaming kernel and its fused all-reduce.
+// Whether the tensor-core kernel serves this context: the default unless the context asks
+// for the streaming kernel (or G4B200_MLP_KERNEL=stream sets the default), on one GPU or
+// on a tensor-parallel context of at most kTcMaxTp ranks that exchange over peer memory
+// and whose shard the kernel's tiles fit (256-k stages of the down projection, 16-byte
+// rows of its scales: TP8's 120-byte rows do not).  The NCCL fallback keeps the
+// streaming kernel.
+constexpr int kTcMaxTp = 1;  // tensor-parallel sizes enabled once run on that many GPUs
 bool mlp_tc_enabled(const g4_ctx* ctx) {
   static const int env_kind = [] {
     const char* e = std::getenv("G4B200_MLP_KERNEL");
@@ -901,8 +975,12 @@ bool mlp_tc_enabled(const g4_ctx* ctx) {
     return static_cast<int>(G4_MLP_TENSOR);
   }();
   const int kind = ctx->mlp_kernel == G4_MLP_AUTO ? env_kind : ctx->mlp_kernel;
-  return kind == G4_MLP_TENSOR && ctx->tp_world == 1 && ctx->buf.tc_seg != nullptr && ctx->buf.tc_ptag != nullptr &&
-         ctx->buf.tc_htag != nullptr;
+  if (kind != G4_MLP_TENSOR || ctx->buf.tc_seg == nullptr || ctx->buf.tc_ptag == nullptr || ctx->buf.tc_htag == nullptr)
+    return false;
+  if (ctx->tp_world == 1) return true;
+  const int lrows = L / ctx->tp_world;
+  return ctx->tp_world <= kTcMaxTp && ctx->peers.world == ctx->tp_world && lrows % tc::kKStage == 0 &&
+         (lrows / 16) % 16 == 0 && lrows % 64 == 0;
 }
 
 g4_status launch_decoder_feedforward_tc(g4_ctx* ctx, uint16_t* residual, const uint16_t* pre_w, const uint8_t* up_p,
@@ -911,7 +989,7 @@ g4_status launch_decoder_feedforward_tc(g4_ctx* ctx, uint16_t* residual, const u
                                         const float* gate_gs, const float* down_gs, const uint16_t* post_w,
                                         const uint16_t* layer_scalar) {
   using namespace tc;
-  const int lrows = L;
+  const int lrows = L / ctx->tp_world;  // this rank's shard of the intermediate rows
   // host check of the partition: every tile has at most kMaxSeg segments
   const int G = ctx->sm_count;
   for (int ph = 0; ph < 2; ++ph) {
@@ -949,6 +1027,7 @@ g4_status launch_decoder_feedforward_tc(g4_ctx* ctx, uint16_t* residual, const u
   a.htag = ctx->buf.tc_htag;
   a.lrows = lrows;
   a.budget_ns = ctx->wait_budget_ns;
+  a.xch = ctx->tp_world > 1 ? ctx->peers : PeerXch{};
   const size_t smem = sizeof(Smem) + 1024;
   g4_status st = allow_max_dynamic_smem(ctx, (const void*)mlp_tc_kernel, smem, "mlp_tc_kernel smem");
   if (st != G4_OK) return st;
