@@ -141,6 +141,47 @@ def test_decoder_feedforward_repeat_and_graph_replay(gpu_ctx, kind):
     gpu_ctx.set_mlp_kernel("auto")
 
 
+def test_decoder_feedforward_switching_kernels_on_one_context(gpu_ctx):
+    """Both MLP kernels share a context's scratch (the down-phase ticket, the tensor-core
+    kernel's launch tag): a chain that switches between them is deterministic -- two
+    contexts running the same sequence agree bit for bit -- and each tensor-core launch
+    after a streaming one still matches a fresh context's result for the same input."""
+    import harness
+
+    c = harness.build_case("decoder_feedforward")
+    base = harness.mlp_tensors(c)
+    seq = ["tensor", "stream", "tensor", "tensor", "stream", "tensor"]
+
+    def chain(ctx):
+        t = dict(base)
+        t["residual"] = base["residual"].clone()
+        outs = []
+        for kind in seq:
+            ctx.set_mlp_kernel(kind)
+            g4.decoder_feedforward(ctx, **t)
+            outs.append(t["residual"].clone())
+        torch.cuda.synchronize()
+        assert ctx.poll() == 0
+        ctx.set_mlp_kernel("auto")
+        return outs
+
+    a = chain(gpu_ctx)
+    other = g4.Context(0)
+    b = chain(other)
+    other.close()
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
+    # one tensor-core step from the chain's input, on a fresh context
+    fresh = g4.Context(0)
+    fresh.set_mlp_kernel("tensor")
+    t = dict(base)
+    t["residual"] = a[1].clone()
+    g4.decoder_feedforward(fresh, **t)
+    torch.cuda.synchronize()
+    assert torch.equal(t["residual"], a[2])
+    fresh.close()
+
+
 def _rand_bf16(gen, shape, std):
     return (torch.randn(shape, generator=gen) * std).to(torch.bfloat16)
 
