@@ -767,7 +767,6 @@ __global__ void __launch_bounds__(kThreads, 1)
               sm.abort_flag = 1;
               break;
             }
-            __nanosleep(128);
           }
           float tot = v;
 #pragma unroll
@@ -792,7 +791,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int len = whole ? P1.S : min(hi - lo, P1.S);
       // One 16-element block of h per thread (len * 16 <= 256 < 320), read as tagged
       // words until every tag is this launch's: no grid barrier, and the words of tiles
-      // already finished arrive in one round trip.  The pieces' reference exponent is the
+      // already finished arrive in one round trip.  Rounds follow each other without a
+      // sleep (a round is already a memory round trip; a sleep only delays the last one).  The pieces' reference exponent is the
       // largest of this CTA's window (each CTA scales its own partial sums).
       const int kl = g >> 4, bs = g & 15;
       const bool mine = g < len * 16;
@@ -818,7 +818,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             sm.abort_flag = 1;
             break;
           }
-          __nanosleep(128);
         }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
