@@ -352,12 +352,12 @@ struct Part {
   }
 };
 
-// Bounded wait on an mbarrier phase.  Only the calling thread polls (no hardware suspend:
-// its wake-up latency shows on every stage of a cold launch); warps wait through
-// warp_wait, where lane 0 polls for everyone, so idle warps add little shared-memory
-// traffic next to the MMA issuer's polling.
+// Bounded wait on an mbarrier phase.  Only the calling thread polls, and it never sleeps
+// (neither a hardware suspend nor __nanosleep: their wake-up latency showed at every phase
+// end -- 0.3 us per launch; this kernel's warps are not issue-bound, so spinning costs
+// nothing); warps wait through warp_wait, where lane 0 polls for everyone.
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Smem& sm, uint32_t* status) {
-  const bool ok = mbar_wait(bar, parity, sm.deadline);
+  const bool ok = mbar_wait(bar, parity, sm.deadline, true);
   if (!ok) {
     sm.abort_flag = 1;
     atomicOr(status, DEV_ERR_TIMEOUT_MBAR);
