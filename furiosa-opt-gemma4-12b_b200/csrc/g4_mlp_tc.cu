@@ -648,7 +648,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         wv[0] = __ldg(reinterpret_cast<const uint4*>(args.pre_w) + 2 * g);
         wv[1] = __ldg(reinterpret_cast<const uint4*>(args.pre_w) + 2 * g + 1);
       }
+      // thread 0's scalars: the global scales (never written) before the wait, the launch
+      // count (written by the previous launch) after it, beside the residual loads
+      float gs_gate = 0.f, gs_up = 0.f;
+      uint32_t launches = 0u;
+      if (g == 0) {
+        gs_gate = __ldg(args.gate_gs);
+        gs_up = __ldg(args.up_gs);
+      }
       pdl_wait();
+      if (g == 0) launches = __ldcg(&args.scr->tc_epoch);
       if (g < nblk) {
         xv[0] = __ldg(reinterpret_cast<const uint4*>(args.residual) + 2 * g);
         xv[1] = __ldg(reinterpret_cast<const uint4*>(args.residual) + 2 * g + 1);
@@ -670,9 +679,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int gmax = static_cast<int>((__float_as_uint(red.y * rf * 1.01f) >> 23) & 0xFFu);
       if (g < kPieces) sm.pw[0][g] = pow2f(gmax - 127 - 2 * g);
       if (g == 0) {
-        sm.gate_gs = __ldg(args.gate_gs);
-        sm.up_gs = __ldg(args.up_gs);
-        sm.tag = __ldcg(&args.scr->tc_epoch) + 1u;  // the previous launch's count (after the wait)
+        sm.gate_gs = gs_gate;
+        sm.up_gs = gs_up;
+        sm.tag = launches + 1u;  // the previous launch's count (read after the wait)
       }
       if (g < nblk) {
         const uint32_t xw[8] = {xv[0].x, xv[0].y, xv[0].z, xv[0].w, xv[1].x, xv[1].y, xv[1].z, xv[1].w};
