@@ -36,7 +36,7 @@ constexpr size_t kHFloats = 15360;                // MLP intermediate (bf16 stor
 constexpr size_t kAttnFloats = 512 * (2 * 16 + 16 * 512) + 4096;  // 512 chunks of 16 heads
 constexpr size_t kTcTiles = 15360 / 64 + 3840 / 128;              // gate/up tiles + down tiles
 constexpr size_t kTcSegFloats = kTcTiles * 8 * 128;               // 8 segment slots of 128 rows
-constexpr size_t kTcPartWords = (15360 / 64) * 8 * 128;           // tagged gate/up segment partials
+constexpr size_t kTcPartWords = kTcTiles * 8 * 128;                // tagged segment partials (both phases)
 
 // Tensor-parallel one-shot all-reduce over peer memory.  Each rank owns one exchange
 // buffer of 64-bit words, word[2][kMaxTp][3840]: two halves used by alternate launches,
@@ -63,9 +63,9 @@ struct DeviceBuffers {
   float* ybuf = nullptr;     // [3840] f32 (TP all-reduce buffer)
   float* attn = nullptr;     // [kAttnFloats] split-KV partials
   uint64_t* xch = nullptr;   // [kXchWords] TP peer exchange (this rank's, IPC-exported)
-  float* tc_seg = nullptr;   // [kTcSegFloats] tensor-core MLP: per-tile segment partials
+  float* tc_seg = nullptr;   // [kTcSegFloats] tensor-core MLP: the down projection's 3840 sums
   // Tensor-core MLP values exchanged between CTAs, each word tagged with the launch that
-  // wrote it (zero at creation): gate/up segment partials {f32, tag} and h {bf16, tag}.
+  // wrote it (zero at creation): segment partials {f32, tag} and h {bf16, tag}.
   uint64_t* tc_ptag = nullptr;  // [kTcPartWords]
   uint32_t* tc_htag = nullptr;  // [kHFloats]
 };

@@ -16,10 +16,10 @@
 // Work split.  Phase p has T tiles of 128 rows x S stages of 256 k.  The T*S (tile, stage)
 // pairs are cut into 148 contiguous ranges (stream-K): CTA c owns pairs
 // [c*W/G, (c+1)*W/G).  A CTA's run inside one tile is a segment; its MMAs accumulate in
-// one of two TMEM accumulators.  Phase 0 finishes a tile (GeGLU -> h) in the CTA holding
-// its first k-stages, adding the other parts' partial sums (k order); phase 1 leaves every
-// segment's 128 partial sums in a per-tile slot and the last CTA to finish adds them in k
-// order and runs the RMSNorm/residual tail.  Values one CTA hands to another inside a
+// one of two TMEM accumulators.  Both phases finish a tile in the CTA holding its first
+// k-stages, adding the other parts' partial sums in k order: phase 0 goes on to GeGLU -> h,
+// phase 1 stores the tile's 128 sums; the last CTA to finish loads the 3840 sums (not every
+// segment's partials) and runs the RMSNorm/residual tail.  Values one CTA hands to another inside a
 // launch (gate/up partial sums, h) are words tagged with the launch's number: a reader
 // re-reads a word until its tag is current, so neither a flag nor a grid barrier stands
 // between the phases, and a value already written costs one round trip.
@@ -96,8 +96,8 @@ struct Args {
   const float* down_gs;
   Scratch* scr;
   float* part;       // [H] down-projection sums
-  float* seg;        // [(T0 + T1) * kMaxSeg * 128] segment partials (down phase)
-  uint64_t* ptag;    // [T0 * kMaxSeg * 128] gate/up segment partials {f32 bits, launch tag}
+  float* seg;        // [H] the down projection's sums (each down tile's 128, k order)
+  uint64_t* ptag;    // [(T0 + T1) * kMaxSeg * 128] segment partials {f32 bits, launch tag}
   uint32_t* htag;    // [L] h {bf16 bits, launch tag in the high half}
   int lrows;         // intermediate rows of this rank's shard
   uint64_t budget_ns;
@@ -724,12 +724,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         st_relaxed_gpu_u32(&args.htag[tile * 64 + m], static_cast<uint32_t>(f32_to_bf16(hv)) | (sm.tag << 16));
       }
     };
-    // Accumulator epilogue of one phase (warps 4..7), segments in the MMA order.  Phase 0:
-    // a whole tile is finished here; a split tile's tail part stores its partial sums as
-    // tagged words; the head part's CTA owns the tile: it reads the other parts' words
-    // (again until their tags are this launch's: one round trip when they are in), adds
-    // the parts in k order and finishes the tile.  Phase 1: partial sums only (the tail
-    // adds them).
+    // Accumulator epilogue of one phase (warps 4..7), segments in the MMA order.  A whole
+    // tile is finished here; a split tile's tail part stores its partial sums as tagged
+    // words; the head part's CTA owns the tile: it reads the other parts' words (again
+    // until their tags are this launch's: one round trip when they are in), adds the parts
+    // in k order and finishes the tile (phase 0: GeGLU -> h; phase 1: the 128 sums).
     auto run_epilogue = [&](int ph) {
       const Part& P = parts[ph];
       const int tbase_idx = (ph == 0) ? 0 : P0.T;
@@ -752,14 +751,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.dempty[buf]);
         ++nseg;
-        float* slots = args.seg + static_cast<size_t>(tbase_idx + tile) * kMaxSeg * 128;
-        uint64_t* tagged = args.ptag + static_cast<size_t>(tile) * kMaxSeg * 128 + m;
-        if (ph == 1) {
-          slots[segi * 128 + m] = v;
-        } else if (segi > 0) {
+        uint64_t* tagged = args.ptag + static_cast<size_t>(tbase_idx + tile) * kMaxSeg * 128 + m;
+        if (segi > 0) {
           st_relaxed_gpu_u64(tagged + segi * 128, (static_cast<uint64_t>(sm.tag) << 32) | __float_as_uint(v));
         } else if (nseg_tile == 1) {
-          geglu_store(tile, v);
+          if (ph == 0) geglu_store(tile, v); else args.seg[tile * 128 + m] = v;
         } else {
           uint64_t w[kMaxSeg];
           for (uint32_t round = 0;; ++round) {  // every part's word re-read each round
@@ -781,7 +777,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int sgi = 1; sgi < kMaxSeg; ++sgi)  // the parts in k order
             if (sgi < nseg_tile) tot += __uint_as_float(static_cast<uint32_t>(w[sgi]));
-          geglu_store(tile, tot);
+          if (ph == 0) geglu_store(tile, tot); else args.seg[tile * 128 + m] = tot;
         }
         named_bar_sync(kBarEpi, 128);
       }
@@ -868,23 +864,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     float t[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     tail_loads();
     if (grp < H / 8) {
-      const int tile = (8 * grp) / 128, m0 = (8 * grp) % 128;
-      const int first_owner = P1.owner(tile * P1.S, G);
-      const int ns = P1.owner(tile * P1.S + P1.S - 1, G) - first_owner + 1;
-      const float4* sp = reinterpret_cast<const float4*>(args.seg + (static_cast<size_t>(P0.T + tile) * kMaxSeg * 128 + m0));
-      float4 pv[kMaxSeg][2];
-#pragma unroll
-      for (int sgi = 0; sgi < kMaxSeg; ++sgi)  // every load issued before the first add
-        if (sgi < ns) {
-          pv[sgi][0] = __ldcg(sp + sgi * 32);
-          pv[sgi][1] = __ldcg(sp + sgi * 32 + 1);
-        }
-#pragma unroll
-      for (int sgi = 0; sgi < kMaxSeg; ++sgi)  // the tile's segments in k order
-        if (sgi < ns) {
-          t[0] += pv[sgi][0].x, t[1] += pv[sgi][0].y, t[2] += pv[sgi][0].z, t[3] += pv[sgi][0].w;
-          t[4] += pv[sgi][1].x, t[5] += pv[sgi][1].y, t[6] += pv[sgi][1].z, t[7] += pv[sgi][1].w;
-        }
+      // every down tile was finished by the CTA holding its first k-stages (its ticket came
+      // after): the 3840 sums, 32 bytes per thread
+      const float4* yp = reinterpret_cast<const float4*>(args.seg) + 2 * grp;
+      const float4 p0 = __ldcg(yp), p1 = __ldcg(yp + 1);
+      t[0] = p0.x, t[1] = p0.y, t[2] = p0.z, t[3] = p0.w, t[4] = p1.x, t[5] = p1.y, t[6] = p1.z, t[7] = p1.w;
     }
     // tensor parallel: every rank's down sums, added in rank order on every rank
     const bool xch_ok = args.xch.world <= 1 || peer_allreduce_tc(args.xch, &args.scr->xch_epoch, t, tid, status, sm);

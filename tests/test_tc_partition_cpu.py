@@ -15,8 +15,8 @@ import pytest
 H, L = 3840, 15360
 K_STAGE, MAX_CTA_SEG, MAX_SEG, MAX_LOCAL = 256, 4, 8, 16
 TC_TILES = L // 64 + H // 128          # kTcTiles
-PART_WORDS = (L // 64) * MAX_SEG * 128  # kTcPartWords
-SEG_FLOATS = TC_TILES * MAX_SEG * 128   # kTcSegFloats
+PART_WORDS = TC_TILES * MAX_SEG * 128   # kTcPartWords (tagged partials of both phases)
+SEG_FLOATS = TC_TILES * MAX_SEG * 128   # kTcSegFloats (the down sums use the first H)
 
 
 class Part:
@@ -68,12 +68,12 @@ def test_last_cta_gets_a_lighter_gate_up_share():
 def test_buffer_indices_stay_in_bounds(tp):
     lrows = L // tp
     P0, P1 = phases(lrows)
-    # tagged gate/up partials: (tile * kMaxSeg + segment) * 128 + row
-    assert (P0.T - 1) * MAX_SEG * 128 + (MAX_SEG - 1) * 128 + 127 < PART_WORDS
+    # tagged partials: ((phase-1 tiles after the gate/up ones) tile * kMaxSeg + segment) * 128 + row
+    assert (P0.T + P1.T - 1) * MAX_SEG * 128 + (MAX_SEG - 1) * 128 + 127 < PART_WORDS
     # tagged h: tile * 64 + row of a gate/up tile; read back per 256-k stage of the down phase
     assert (P0.T - 1) * 64 + 63 < L and P1.S * K_STAGE <= L
-    # down-phase partials follow the gate/up tiles' slots
-    assert (P0.T + P1.T - 1) * MAX_SEG * 128 + (MAX_SEG - 1) * 128 + 127 < SEG_FLOATS
+    # the down projection's sums: tile * 128 + row of a down tile
+    assert (P1.T - 1) * 128 + 127 < H <= SEG_FLOATS
     # TMA: 16-byte rows of the down projection's scales, 128-byte boxes of its codes
     assert (lrows // 16) % 16 == 0 and (lrows // 2) % 128 == 0
     # the whole down phase is staged at once when it fits the resident pieces
