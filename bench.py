@@ -137,7 +137,7 @@ class ClockSampler:
 
 def make_layers(device: str, rank: int, world: int):
     import torch
-    from g4b200 import quant, tp
+    from g4formats import quant, tp
 
     layers = []
     for i in range(NLAYERS):
@@ -195,6 +195,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     with torch.cuda.graph(graph, stream=stream):
         for i in range(NLAYERS):
             step(i)
+    stream.synchronize()
+    # replay the captured round a few times before timing: the first replays after capture
+    # pay one-off costs (graph upload, instruction cache) that a long run never sees
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            graph.replay()
     stream.synchronize()
     rounds, rem = divmod(args.steps, NLAYERS)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -302,55 +308,50 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "device_status": status,
     }
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args.cpu_budget)
+        line["cpu_baseline"] = cpu_baseline(args)
     return line
 
 
-def cpu_baseline(budget_s: float) -> dict:
-    """The reference's PyTorch CPU path (oracle port) on this host, bounded sample."""
+def _cpu_reference_tokens(steps: int, warmup: int, budget_s: float) -> tuple[float, int, int]:
+    """The reference's PyTorch CPU decoder_feedforward (oracle/cpu_reference.py) on this
+    host's cores, config-1 layer-0 inputs built by g4formats (library-free: the product
+    library is not loaded).  Both CPU legs use this one method: `warmup` tokens, then up
+    to `steps` tokens timed one by one, median."""
     sys.path.insert(0, str(ROOT))
-    import torch
-
-    from g4b200 import quant
+    from g4formats import quant
     from oracle import cpu_reference
 
     m = quant.mlp_config1(seed=0, device="cpu")
     ref = cpu_reference.ReferenceFeedforward(m)
-    med, n, threads = cpu_reference.time_tokens(ref, m["residual"], budget_s=budget_s)
+    return cpu_reference.time_tokens(ref, m["residual"], steps=steps, warmup=warmup, budget_s=budget_s)
+
+
+def cpu_baseline(args) -> dict:
+    """The reference's PyTorch CPU path (oracle port) on this host, bounded sample."""
+    med, n, threads = _cpu_reference_tokens(args.steps, min(args.warmup, 5), args.cpu_budget)
     return {"value": round(med * 1e6, 1), "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{n} tokens of decoder_feedforward (config 1, layer 0), median, torch CPU bf16 "
-                      f"GloballyScaled MLP as in scripts/generate_references.py:588-639"}
+            "sample": f"{n} tokens of decoder_feedforward (config 1, layer 0) after {min(args.warmup, 5)} warm-up, "
+                      f"median, torch CPU bf16 GloballyScaled MLP as in scripts/generate_references.py:588-639"}
 
 
 def run_reference(args, rank: int, world: int) -> dict | None:
+    """`--impl reference`: the reference's CPU implementation of the path (the oracle
+    port; the reference itself is Rust for an NPU and cannot run here), timed exactly
+    like this arm's `cpu_baseline`.  Imports only g4formats and oracle/, never g4b200."""
     if rank != 0:
         return None
-    sys.path.insert(0, str(ROOT))
-    import torch
-
-    from g4b200 import quant
-    from oracle import cpu_reference
-
-    m = quant.mlp_config1(seed=0, device="cpu")
-    ref = cpu_reference.ReferenceFeedforward(m)
-    torch.set_num_threads(os.cpu_count() or 1)
-    x = m["residual"]
-    for _ in range(max(1, min(args.warmup, 3))):
-        ref(x)
-    steps = max(1, min(args.steps, args.ref_steps))
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        ref(x)
-    dt = (time.perf_counter() - t0) / steps
-    v = round(dt * 1e6, 1)
+    med, n, threads = _cpu_reference_tokens(args.steps, min(args.warmup, 5), args.cpu_budget)
+    v = round(med * 1e6, 1)
     return {
-        "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": args.warmup,
-        "ms_per_step": round(dt * 1e3, 3), "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+        "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": n, "warmup": args.warmup,
+        "ms_per_step": round(med * 1e3, 4), "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16 (dequantised NVFP4 weights), CPU", "data": "synthetic (same as ours)", "impl": "reference",
+        "same_steps": n == args.steps,
         "config": {"workload": "decoder_feedforward one token, BASELINE config 1 (H=3840, L=15360, NVFP4)",
                    "global_batch": 1, "seq_len": 1, "parallelism": "cpu"},
-        "cpu_baseline": {"value": v, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-                         "sample": f"{steps} tokens, layer-0 weights, torch CPU GloballyScaled MLP"},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{n} tokens (median) after {min(args.warmup, 5)} warm-up, layer-0 weights, "
+                                   f"torch CPU GloballyScaled MLP"},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -361,8 +362,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-budget", type=float, default=15.0)
-    ap.add_argument("--ref-steps", type=int, default=10)
+    ap.add_argument("--cpu-budget", type=float, default=30.0, help="seconds: cap of each CPU leg's timed tokens")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mlp-kernel", choices=["auto", "stream", "tensor"], default="auto",
                     help="decoder_feedforward kernel: streaming (CUDA-core decode) or tcgen05 (one GPU)")

@@ -35,7 +35,7 @@ constexpr size_t kHeadFloats = 8192 + 512 + 8192; // raw projection rows (qkv)
 constexpr size_t kHFloats = 15360;                // MLP intermediate (bf16 stored)
 constexpr size_t kAttnFloats = 512 * (2 * 16 + 16 * 512) + 4096;  // 512 chunks of 16 heads
 constexpr size_t kTcTiles = 15360 / 64 + 3840 / 128;              // gate/up tiles + down tiles
-constexpr size_t kTcSegFloats = kTcTiles * 8 * 128;               // 8 segment slots of 128 rows
+constexpr size_t kTcSegFloats = 3840;                             // the down projection's H sums
 constexpr size_t kTcPartWords = kTcTiles * 8 * 128;                // tagged segment partials (both phases)
 
 // Tensor-parallel one-shot all-reduce over peer memory.  Each rank owns one exchange

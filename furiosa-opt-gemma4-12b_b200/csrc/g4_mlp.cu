@@ -338,37 +338,43 @@ static_assert(kNoAllocBytes == G4_NOALLOC_SCRATCH_BYTES, "header states the arra
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
 struct NoAllocDevice {
-  std::once_flag once;
-  cudaError_t err = cudaSuccess;
-  const char* what = "";
+  bool ready = false;             // set up successfully (a failed set-up is retried)
   unsigned char* base = nullptr;  // this device's address of g_noalloc_scratch
   int sm_count = 0;
-  int smem_optin = 0;
+  int smem_dyn_max = 0;           // dynamic shared memory mlp_kernel may use per launch
   bool coop = false;
 };
 constexpr int kNoAllocMaxDevices = 64;
 NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;
 
-// Once per device, with that device current.  Allocates nothing: the array belongs to
-// the module image the runtime loaded on this device.
-void noalloc_setup(NoAllocDevice& d, int dev) {
+// Once per device, with that device current (under g_noalloc_mu; a failure leaves the
+// device not ready, so the next call tries again).  Allocates nothing: the array belongs
+// to the module image the runtime loaded on this device.  It also raises mlp_kernel's
+// dynamic shared-memory limit to the opt-in maximum minus the kernel's static shared
+// memory: the same value the context path sets, so neither path lowers it under the other.
+cudaError_t noalloc_setup(NoAllocDevice& d, int dev) {
   void* ptr = nullptr;
   cudaError_t e = cudaGetSymbolAddress((void**)&ptr, g_noalloc_scratch);
-  if (e != cudaSuccess) {
-    d.err = e;
-    d.what = "cudaGetSymbolAddress(g_noalloc_scratch)";
-    return;
-  }
-  int coop = 0;
-  if ((e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
-      (e = cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess ||
-      (e = cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev)) != cudaSuccess) {
-    d.err = e;
-    d.what = "cudaDeviceGetAttribute";
-    return;
-  }
+  if (e != cudaSuccess) return e;
+  int coop = 0, optin = 0, sms = 0;
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
+      (e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess ||
+      (e = cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev)) != cudaSuccess)
+    return e;
+  cudaFuncAttributes fa = {};
+  if ((e = cudaFuncGetAttributes(&fa, (const void*)g4::mlp_kernel)) != cudaSuccess) return e;
+  const int dyn_max = optin - static_cast<int>(fa.sharedSizeBytes);
+  if (dyn_max <= 0) return cudaErrorInvalidConfiguration;
+  if ((e = cudaFuncSetAttribute((const void*)g4::mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn_max)) !=
+      cudaSuccess)
+    return e;
+  d.sm_count = sms;
+  d.smem_dyn_max = dyn_max;
   d.coop = coop != 0;
   d.base = static_cast<unsigned char*>(ptr);
+  d.ready = true;
+  return cudaSuccess;
 }
 
 bool noalloc_aligned(const void* p, uintptr_t a) {
@@ -394,8 +400,9 @@ extern "C" g4_status g4_decoder_feedforward_noalloc(
   op.dq = static_cast<int>(dq);
   op.g0 = make_geom(Fmt::NVFP4, H / 2, 1);
   op.g1 = make_geom(Fmt::NVFP4, n / 2u / dq, dq);
-  if (n % 128u != 0u || !geom_ok(op.g0, H / 2, H / 16) || !geom_ok(op.g1, n / 2u, n / 16u))
-    return G4_ERR_UNSUPPORTED;
+  // the shapes the kernel's down-phase geometry is built and tested for
+  const bool shape_ok = (n <= 3840u && n % 128u == 0u) || n == 7680u || n == 15360u;
+  if (!shape_ok || !geom_ok(op.g0, H / 2, H / 16) || !geom_ok(op.g1, n / 2u, n / 16u)) return G4_ERR_UNSUPPORTED;
   const void* p16[] = {residual, pre_ff_rms_weight, up_weight_packed, gate_weight_packed, down_weight_packed,
                        up_weight_scale, gate_weight_scale, down_weight_scale, post_ff_rms_weight, layer_scalar};
   for (const void* p : p16)
@@ -408,14 +415,19 @@ extern "C" g4_status g4_decoder_feedforward_noalloc(
   if (cudaGetDevice(&dev) != cudaSuccess) return G4_ERR_CUDA;
   if (dev < 0 || dev >= kNoAllocMaxDevices) return G4_ERR_UNSUPPORTED;
   NoAllocDevice& d = g_noalloc_dev[dev];
-  std::call_once(d.once, noalloc_setup, std::ref(d), dev);
-  if (d.err != cudaSuccess || d.base == nullptr) return G4_ERR_CUDA;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!d.ready && noalloc_setup(d, dev) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return G4_ERR_CUDA;
+    }
+  }
   if (!d.coop) return G4_ERR_UNSUPPORTED;
 
   const uint32_t slot_bytes = op.g0.slot_bytes > op.g1.slot_bytes ? op.g0.slot_bytes : op.g1.slot_bytes;
   const uint32_t x_bytes = (n * 2u > static_cast<uint32_t>(H) * 4u) ? n * 2u : static_cast<uint32_t>(H) * 4u;
   const StreamLayout lay = make_layout(slot_bytes, kMlpSlots, x_bytes);
-  if (lay.total > static_cast<uint32_t>(d.smem_optin)) return G4_ERR_UNSUPPORTED;
+  if (lay.total > static_cast<uint32_t>(d.smem_dyn_max)) return G4_ERR_UNSUPPORTED;
 
   op.residual = residual;
   op.pre_w = pre_ff_rms_weight;
@@ -436,10 +448,6 @@ extern "C" g4_status g4_decoder_feedforward_noalloc(
   op.ybuf = nullptr;
   op.xch = PeerXch{};
 
-  // The opt-in maximum, never lower: the context path sets this attribute once per
-  // device for its own (possibly larger) layout and must keep working after us.
-  if (cudaFuncSetAttribute(mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, d.smem_optin) != cudaSuccess)
-    return G4_ERR_CUDA;
   // The counters and status word must start at zero; a call that gave up on a device
   // wait may have left them set.
   if (cudaMemsetAsync(d.base, 0, sizeof(Scratch), stream) != cudaSuccess) return G4_ERR_CUDA;

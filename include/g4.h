@@ -274,8 +274,11 @@ g4_status g4_sliding_attention_output_nvfp4(g4_ctx* ctx, const g4_bf16* x,
 #define G4_NOALLOC_MAX_INTERMEDIATE 15360 /* rows of up/gate = K of down       */
 #define G4_NOALLOC_SCRATCH_BYTES 47104    /* 46 KiB: 1 KiB counters, f32 [H], bf16 [max intermediate] */
 
-/* The decoder_feedforward math of g4_decoder_feedforward (same formula, same kernel,
- * in place on residual[H]) for callers that cannot allocate device memory.  It has no
+/* The decoder_feedforward math of g4_decoder_feedforward (same formula, in place on
+ * residual[H]) for callers that cannot allocate device memory.  It always runs the
+ * streaming kernel (CUDA-core NVFP4 decode + mma.sync, the kernel a context runs with
+ * G4_MLP_STREAM), whose scratch fits the fixed array below; a single-GPU context
+ * defaults to the tcgen05 kernel, so the two agree within f32 rounding, not bit for bit.  It has no
  * counterpart in the reference.  A g4_ctx needs cudaMalloc for its scratch, which some
  * hosts do not allow: serving engines that hand every free byte of HBM to their own
  * pool at start-up (a later cudaMalloc fails or fragments that pool), plugin hooks that
@@ -285,10 +288,10 @@ g4_status g4_sliding_attention_output_nvfp4(g4_ctx* ctx, const g4_bf16* x,
  * vector h) in the fixed array above and calls no allocating routine.
  *
  *   stream            : a stream of the CURRENT device (NULL = its default stream).
- *   intermediate_size : rows of up/gate and K of down.  G4_L for the model's layer;
- *                       also 7680, or a multiple of 128 up to 3840 (single-GPU only,
+ *   intermediate_size : rows of up/gate and K of down: exactly G4_L (the model's
+ *                       layer), 7680, or a multiple of 128 up to 3840 (single-GPU only,
  *                       no all-reduce).  > G4_NOALLOC_MAX_INTERMEDIATE returns
- *                       G4_ERR_TOO_LARGE; other shapes return G4_ERR_UNSUPPORTED.
+ *                       G4_ERR_TOO_LARGE; every other size returns G4_ERR_UNSUPPORTED.
  *   weights           : as g4_decoder_feedforward with L = intermediate_size
  *                       (up/gate [n, H/2] codes, [n, H/16] scales; down [H, n/2] codes,
  *                       [H, n/16] scales).

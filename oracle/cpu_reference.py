@@ -79,16 +79,20 @@ class ReferenceFeedforward:
         return ((residual + hidden).to(torch.bfloat16) * self.layer_scalar).to(torch.bfloat16)
 
 
-def time_tokens(ref: ReferenceFeedforward, x: torch.Tensor, budget_s: float = 15.0, max_tokens: int = 64,
-                warmup: int = 2):
-    """Median per-token seconds over a bounded sample; returns (median_s, tokens, threads)."""
+def time_tokens(ref: ReferenceFeedforward, x: torch.Tensor, steps: int, warmup: int = 3,
+                budget_s: float = 30.0):
+    """Per-token CPU time of `ref`, the one timing method of both CPU legs of bench.py.
+
+    `warmup` untimed tokens, then `steps` tokens timed one by one with perf_counter,
+    stopping early only when `budget_s` seconds have passed (at least 3 tokens).
+    Returns (median_s, tokens_timed, threads); all host threads are used."""
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    for _ in range(warmup):
+    for _ in range(max(0, warmup)):
         ref(x)
     times = []
     t_end = time.perf_counter() + budget_s
-    while len(times) < max_tokens and (len(times) < 3 or time.perf_counter() < t_end):
+    while len(times) < steps and (len(times) < 3 or time.perf_counter() < t_end):
         t0 = time.perf_counter()
         ref(x)
         times.append(time.perf_counter() - t0)

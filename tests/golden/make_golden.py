@@ -16,7 +16,7 @@ class.  The vision/audio classes are stubs because the vision/audio generators a
 not run (they are outside the text hot path).  `verify_rope_matches_upstream`
 (generate_references.py:273-290) still runs and guards the RoPE table convention.
 
-Usage:  python tests/golden/make_golden.py [/path/to/reference]
+Usage:  python tests/golden/make_golden.py <reference checkout>   (or G4B200_REFERENCE_DIR=...)
 """
 
 import sys
@@ -87,7 +87,12 @@ def bf16_bits(t: torch.Tensor) -> np.ndarray:
 
 
 def main() -> None:
-    reference = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    import os
+
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("G4B200_REFERENCE_DIR")
+    if not ref:
+        raise SystemExit("usage: make_golden.py <reference checkout> (or set G4B200_REFERENCE_DIR)")
+    reference = Path(ref)
     scripts = reference / "scripts"
     if not (scripts / "generate_references.py").exists():
         raise SystemExit(f"reference generator not found under {scripts}")

@@ -7,7 +7,7 @@ import pytest
 import torch
 
 import g4b200 as g4
-from g4b200 import quant
+from g4formats import quant
 from oracle import cases, ops, prng
 
 pytestmark = pytest.mark.gpu

@@ -16,7 +16,7 @@ H, L = 3840, 15360
 K_STAGE, MAX_CTA_SEG, MAX_SEG, MAX_LOCAL = 256, 4, 8, 16
 TC_TILES = L // 64 + H // 128          # kTcTiles
 PART_WORDS = TC_TILES * MAX_SEG * 128   # kTcPartWords (tagged partials of both phases)
-SEG_FLOATS = TC_TILES * MAX_SEG * 128   # kTcSegFloats (the down sums use the first H)
+SEG_FLOATS = H                          # kTcSegFloats: the down projection's H sums
 
 
 class Part:

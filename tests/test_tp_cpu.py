@@ -1,5 +1,5 @@
 """Tensor-parallel host logic on CPU: two `gloo` ranks shard one NVFP4 GeGLU MLP the way
-the library expects a rank's weights (g4b200.tp.shard_mlp: gate/up rows, down K-slice
+the library expects a rank's weights (g4formats.tp.shard_mlp: gate/up rows, down K-slice
 on 16-element scale-block boundaries), each computes its part with the oracle, and the
 all-reduced partial down projection must equal the unsharded one.  Small shapes: the
 sharding code takes the model dimensions as arguments."""
@@ -12,7 +12,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from g4b200 import quant, tp
+from g4formats import quant, tp
 from oracle import ops
 
 HS, LS = 256, 512  # hidden / intermediate sizes of the test MLP

@@ -61,7 +61,7 @@ def _rank(rank: int, world: int, port: int, q) -> None:
     import torch.distributed as dist
 
     import g4b200 as g4
-    from g4b200 import quant, tp
+    from g4formats import quant, tp
 
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,

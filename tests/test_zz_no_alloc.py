@@ -12,7 +12,7 @@ import pytest
 import torch
 
 import g4b200 as g4
-from g4b200 import quant
+from g4formats import quant
 from oracle import cases, ops
 
 MLP_ARGS = ("residual", "pre_ff_rms_weight", "up_weight_packed", "gate_weight_packed", "down_weight_packed",
@@ -39,6 +39,8 @@ def test_rejects_intermediate_beyond_scratch_limit():
 def test_rejects_unsupported_shapes_and_null_pointers():
     assert _raw(11520) == 5  # 3 K-segments per down row: not built
     assert _raw(200) == 5    # not a multiple of 128
+    assert _raw(5120) == 5   # between 3840 and 7680: not a built down-phase geometry
+    assert _raw(3968) == 5
     assert _raw(0) == 1
     assert _raw(15360) == 1  # null pointers
 
