@@ -269,6 +269,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
     del e2e_graphs
 
+    decode = None
+    if not args.no_decode:
+        try:
+            decode = run_decode(args, ctx, stream, rank, world, dev)
+        except Exception as e:  # the headline MLP line still prints
+            decode = {"error": f"{type(e).__name__}: {e}"}
     vals = torch.tensor([total_ms / args.steps, kernel_ms, e2e_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
@@ -307,6 +313,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "clocks": sampler.summary(),
         "device_status": status,
     }
+    if decode is not None:
+        line["decode"] = decode
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args)
     return line
@@ -324,6 +332,109 @@ def _cpu_reference_tokens(steps: int, warmup: int, budget_s: float) -> tuple[flo
     m = quant.mlp_config1(seed=0, device="cpu")
     ref = cpu_reference.ReferenceFeedforward(m)
     return cpu_reference.time_tokens(ref, m["residual"], steps=steps, warmup=warmup, budget_s=budget_s)
+
+
+# per-token algorithmic bytes of the whole-model decode step (TP1): every projection's
+# weights once, the lm_head (the tied embedding table) once, and the KV rows attended
+SLIDING_W = 31_473_664 + 15_736_320       # FP8 q/k/v + o-proj codes and row scales
+FULL_W = 33_440_768 + 31_464_960
+MLP_W = WEIGHT_BYTES + 12
+LM_HEAD_W = 262144 * H * 2
+
+
+def decode_bytes_per_token(n_layers: int, ctx_len: int, world: int) -> int:
+    total = 0
+    for i in range(n_layers):
+        if i % 6 == 5:  # full (MQA) layer: the single K/V head is replicated on every rank
+            total += FULL_W // world + MLP_W // world + min(ctx_len, 32768) * 512 * 2 * 2
+        else:           # sliding: the rank's heads of the 1024-slot ring
+            total += SLIDING_W // world + MLP_W // world + min(ctx_len, 1024) * 8 // world * 256 * 2 * 2
+    return total + LM_HEAD_W // world
+
+
+def run_decode(args, ctx, stream, rank: int, world: int, dev: str) -> dict:
+    """BASELINE config 4 at batch 1: whole-model greedy decode (48 layers, 5 sliding : 1
+    full) through the decode runtime, `decode_tokens` steps after a context of
+    `decode_context` positions.  The KV caches of the context are filled with synthetic
+    unit-RMS rows (the bytes each step reads do not depend on their values); each step is
+    one replay of the captured step graph, position and token kept on the device."""
+    import torch
+    import torch.distributed as dist
+    from cuda.bindings import runtime as cudart
+
+    from g4b200 import runtime
+    from g4formats import model as fm
+
+    n_layers, ctx_len, n_new, warm = 48, args.decode_context, args.decode_tokens, 4
+    t_build = time.time()
+    m = fm.synthetic_model(n_layers, seed=7, device=dev, post_norm=0.05, layer_scalar=(1.0, 1.0))
+    m = fm.shard_model(m, rank, world)
+    rm = runtime.model_from_synthetic(m)
+    ws = runtime.Workspace(ctx, rm, ctx_len + warm + n_new + 8)
+    biggest = max(ws.kv_cache_ptrs(i)[2] for i in range(n_layers))
+    fill = (fm.uniform("kv", 7, biggest // 2, dev) * 3.0 ** 0.5).to(torch.bfloat16)
+    for i in range(n_layers):
+        k, v, nb = ws.kv_cache_ptrs(i)
+        for ptr in (k, v):
+            cudart.cudaMemcpy(ptr, fill.data_ptr(), nb, cudart.cudaMemcpyKind.cudaMemcpyDeviceToDevice)
+    torch.cuda.synchronize()
+    build_s = time.time() - t_build
+    tok = 4242
+    ws.begin([tok], ctx_len, warm + n_new)
+    ws.steps(warm)  # the first captures the step graph
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(int(dev.split(":")[1]))
+    with sampler:
+        t0.record(stream)
+        ws.steps(n_new)
+        t1.record(stream)
+        stream.synchronize()
+    dev_ms = t0.elapsed_time(t1) / n_new
+    toks = ws.tokens(warm + n_new)
+    # end to end through the public call: prompt token from the host, the step graph
+    # replayed per token, the generated ids copied back
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    gen = ws.generate([tok], n_new, start_pos=ctx_len)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / n_new
+    vals = torch.tensor([dev_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    dev_ms, e2e_ms = vals.tolist()
+    status = ctx.poll()
+    ws.close()
+    rm.close()
+    del m
+    peak, peak_kind = measured_peaks()
+    nbytes = decode_bytes_per_token(n_layers, ctx_len + warm + n_new // 2, world)
+    achieved = nbytes / (dev_ms * 1e-3) / 1e9
+    return {
+        "metric": "decode tokens/s", "value": round(1000.0 / dev_ms, 2), "unit": "tokens/s",
+        "us_per_token": round(dev_ms * 1000.0, 2), "higher_is_better": True, "n_gpus": world,
+        "config": {"workload": "whole-model greedy decode, BASELINE config 4 (48 layers: 40 sliding-1024 + 8 full, "
+                               "5:1), batch 1", "context": ctx_len, "decode_steps": n_new, "warmup_steps": warm,
+                   "parallelism": f"tp{world}", "weights": "FP8 attention (reference formats), NVFP4 MLP, bf16 "
+                                                          "tied lm_head; seeded random init, 48 distinct layers",
+                   "kv": "caches filled with synthetic rows for the context", "l2": "inputs larger than L2 "
+                         f"({nbytes / 1e9:.2f} GB streamed per token)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                     "algorithmic_bytes_per_token": nbytes},
+        "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "tokens/s", "us_per_token": round(e2e_ms * 1000.0, 2),
+                "h2d_bytes_per_step": round(4 / n_new, 3), "d2h_bytes_per_step": 4,
+                "launch": "g4_generate_greedy: prompt id H2D, one step-graph replay per token, ids D2H"},
+        "clocks": sampler.summary(), "device_status": status,
+        "tokens_sample": toks[warm:warm + 8], "build_s": round(build_s, 1),
+    }
 
 
 def cpu_baseline(args) -> dict:
@@ -364,6 +475,9 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=30.0, help="seconds: cap of each CPU leg's timed tokens")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the whole-model decode measurement")
+    ap.add_argument("--decode-context", type=int, default=4096)
+    ap.add_argument("--decode-tokens", type=int, default=64)
     ap.add_argument("--mlp-kernel", choices=["auto", "stream", "tensor"], default="auto",
                     help="decoder_feedforward kernel: streaming (CUDA-core decode) or tcgen05 (one GPU)")
     args = ap.parse_args()

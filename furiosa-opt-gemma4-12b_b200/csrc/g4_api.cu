@@ -118,6 +118,14 @@ g4_status allreduce_f32(g4_ctx* ctx, float* buf, size_t count) {
   return G4_OK;
 }
 
+g4_status allgather_u64(g4_ctx* ctx, const uint64_t* in, uint64_t* out) {
+  if (ctx->comm == nullptr || !nccl().ok) return fail(ctx, G4_ERR_NCCL, "tensor parallelism without a communicator");
+  const ncclResult_t r =
+      nccl().all_gather(in, out, 1, ncclUint64, reinterpret_cast<ncclComm_t>(ctx->comm), ctx->stream);
+  if (r != ncclSuccess) return fail(ctx, G4_ERR_NCCL, std::string("ncclAllGather: ") + nccl().error_string(r));
+  return G4_OK;
+}
+
 // Maps every rank's TP exchange buffer into this process (CUDA IPC handles swapped with
 // an NCCL all-gather), so that the MLP and o-proj kernels all-reduce their partial
 // outputs themselves over NVLink.  The ranks then agree (NCCL min) on whether all of
@@ -196,7 +204,7 @@ static g4_status setup_peer_exchange(g4_ctx* ctx) {
 g4_status launch_qkv(g4_ctx*, bool, bool, const uint16_t*, const uint8_t* const[3], const uint8_t* const[3],
                      const uint16_t* const[3], const float* const[3], const uint16_t*, const uint16_t*,
                      const uint16_t*, const int32_t*, const int32_t*, const uint16_t*, const uint16_t*, uint16_t*,
-                     uint16_t*, uint16_t*);
+                     uint16_t*, uint16_t*, long long);
 g4_status launch_oproj(g4_ctx*, bool, bool, const uint16_t*, const float*, const uint16_t*, const uint8_t*,
                        const uint8_t*, const uint16_t*, const float*, uint16_t*);
 g4_status launch_lm_head(g4_ctx*, const uint16_t*, const uint16_t*, const uint16_t*, uint16_t*);
@@ -207,6 +215,8 @@ g4_status launch_full_page(g4_ctx*, bool, const uint16_t*, const uint16_t*, cons
 g4_status launch_full_paged(g4_ctx*, const uint16_t*, const uint16_t* const*, const uint16_t* const*, int, int,
                             float*, uint16_t*);
 g4_status launch_embed(g4_ctx*, const uint16_t*, const int32_t*, uint16_t*);
+g4_status launch_gqa_attention(g4_ctx*, const uint16_t*, const uint16_t*, const uint16_t*, const float*, int,
+                               uint16_t*);
 g4_status launch_argmax(g4_ctx*, const uint16_t*, int, int32_t*);
 g4_status launch_dequant_nvfp4(g4_ctx*, const uint8_t*, const uint8_t*, int, int, uint16_t*);
 g4_status launch_dequant_fp8(g4_ctx*, const uint8_t*, long long, uint16_t*);
@@ -398,7 +408,7 @@ g4_status g4_sliding_project_qkv(g4_ctx* ctx, const g4_bf16* x, const g4_f8e4m3*
   const uint16_t* rs[3] = {q_weight_scale, k_weight_scale, v_weight_scale};
   const float* gs[3] = {nullptr, nullptr, nullptr};
   return launch_qkv(ctx, false, false, x, w, bs, rs, gs, input_rms_weight, q_rms_weight, k_rms_weight, kv_offset,
-                    rope_offset, cos, sin, k_cache, v_cache, q_out);
+                    rope_offset, cos, sin, k_cache, v_cache, q_out, 0);
 }
 
 g4_status g4_sliding_project_qkv_nvfp4(g4_ctx* ctx, const g4_bf16* x, const g4_f4x2* q_weight,
@@ -419,7 +429,7 @@ g4_status g4_sliding_project_qkv_nvfp4(g4_ctx* ctx, const g4_bf16* x, const g4_f
   const uint16_t* rs[3] = {nullptr, nullptr, nullptr};
   const float* gs[3] = {q_global_scale, k_global_scale, v_global_scale};
   return launch_qkv(ctx, false, true, x, w, bs, rs, gs, input_rms_weight, q_rms_weight, k_rms_weight, kv_offset,
-                    rope_offset, cos, sin, k_cache, v_cache, q_out);
+                    rope_offset, cos, sin, k_cache, v_cache, q_out, 0);
 }
 
 g4_status g4_full_project_qkv(g4_ctx* ctx, const g4_bf16* x, const g4_f8e4m3* q_weight, const g4_f8e4m3* k_weight,
@@ -437,7 +447,35 @@ g4_status g4_full_project_qkv(g4_ctx* ctx, const g4_bf16* x, const g4_f8e4m3* q_
   const uint16_t* rs[3] = {q_weight_scale, k_weight_scale, nullptr};
   const float* gs[3] = {nullptr, nullptr, nullptr};
   return launch_qkv(ctx, true, false, x, w, bs, rs, gs, input_rms_weight, q_rms_weight, k_rms_weight, kv_offset,
-                    rope_offset, cos, sin, k_cache, v_cache, q_out);
+                    rope_offset, cos, sin, k_cache, v_cache, q_out, 0);
+}
+
+g4_status g4_full_project_qkv_nvfp4(g4_ctx* ctx, const g4_bf16* x, const g4_f4x2* q_weight, const g4_f4x2* k_weight,
+                                    const g4_f8e4m3* q_block_scale, const g4_f8e4m3* k_block_scale,
+                                    const float* q_global_scale, const float* k_global_scale,
+                                    const g4_bf16* input_rms_weight, const g4_bf16* q_rms_weight,
+                                    const g4_bf16* k_rms_weight, const int32_t* kv_offset, const int32_t* rope_offset,
+                                    const g4_bf16* cos, const g4_bf16* sin, g4_bf16* k_cache, g4_bf16* v_cache,
+                                    g4_bf16* q_out) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, x, q_weight, k_weight, q_block_scale, k_block_scale, input_rms_weight, q_rms_weight,
+                  k_rms_weight, cos, sin, k_cache, v_cache, q_out);
+  G4_REQUIRE_SCALARS(ctx, q_global_scale, k_global_scale, kv_offset, rope_offset);
+  const uint8_t* w[3] = {q_weight, k_weight, nullptr};
+  const uint8_t* bs[3] = {q_block_scale, k_block_scale, nullptr};
+  const uint16_t* rs[3] = {nullptr, nullptr, nullptr};
+  const float* gs[3] = {q_global_scale, k_global_scale, nullptr};
+  return launch_qkv(ctx, true, true, x, w, bs, rs, gs, input_rms_weight, q_rms_weight, k_rms_weight, kv_offset,
+                    rope_offset, cos, sin, k_cache, v_cache, q_out, 0);
+}
+
+g4_status g4_attention_gqa(g4_ctx* ctx, const g4_bf16* q, const g4_bf16* k, const g4_bf16* v, const float* mask,
+                           int n_rows, g4_bf16* out) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, q, k, v, mask, out);
+  if (n_rows < 64 || n_rows > G4_E || n_rows % 64 != 0)
+    return fail(ctx, G4_ERR_BAD_ARG, "n_rows must be a multiple of 64 in [64, 32768]");
+  return launch_gqa_attention(ctx, q, k, v, mask, n_rows, out);
 }
 
 g4_status g4_sliding_attention(g4_ctx* ctx, const g4_bf16* q, const g4_bf16* k, const g4_bf16* v, const float* mask,
@@ -463,6 +501,17 @@ g4_status g4_sliding_attention_output_nvfp4(g4_ctx* ctx, const g4_bf16* x, const
   G4_REQUIRE_PTRS(ctx, x, post_attn_rms_weight, o_weight, o_block_scale, residual);
   G4_REQUIRE_SCALARS(ctx, o_global_scale);
   return launch_oproj(ctx, false, true, x, nullptr, post_attn_rms_weight, o_weight, o_block_scale, nullptr,
+                      o_global_scale, residual);
+}
+
+g4_status g4_full_attention_output_nvfp4(g4_ctx* ctx, const g4_bf16* x, const float* running_sum,
+                                         const g4_bf16* post_attn_rms_weight, const g4_f4x2* o_weight,
+                                         const g4_f8e4m3* o_block_scale, const float* o_global_scale,
+                                         g4_bf16* residual) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, x, post_attn_rms_weight, o_weight, o_block_scale, residual);
+  G4_REQUIRE_SCALARS(ctx, running_sum, o_global_scale);
+  return launch_oproj(ctx, true, true, x, running_sum, post_attn_rms_weight, o_weight, o_block_scale, nullptr,
                       o_global_scale, residual);
 }
 

@@ -1,16 +1,18 @@
-// Decode attention (one query token), split-KV ("flash decoding") on the CUDA cores in
-// f32: scores, exp and the weighted value sum match the reference's f32 softmax
+// Decode attention (one query token), split-KV ("flash decoding"), f32 softmax: scores,
+// exp and the weighted value sum follow the reference's f32 softmax
 // (scripts/generate_references.py:324-330, 436-455, 532-556).
 //
-//  sliding_attention            (src/ops.rs:126-136): GQA 2 q heads per kv head over the
-//      1024-slot ring; one CTA per (kv head, 64-slot chunk); slots whose mask is 0 are
-//      skipped (no K/V bytes read); the last chunk of a head merges the partials.
+//  sliding_attention            (src/ops.rs:126-136): GQA, 2 q heads per kv head over the
+//      1024-slot ring, on the CUDA cores; one CTA per (kv head, 64-slot chunk), 16-byte
+//      loads of every valid slot's K and V issued up front; slots whose mask is 0 are not
+//      read; the last chunk of a head merges the partials.
 //  full_attention_first_page /  (src/ops.rs:160-186, src/device/full/attention.rs:200-334):
-//  full_attention_page           one 512-row page per call, 8 chunks, the last chunk
-//      merges them with the running max/sum/out state (unnormalised out, bf16).
-//  full_attention_paged         every page of a layer in one cooperative launch: CTAs
-//      take chunks, a bounded grid wait, then every CTA merges a slice of the 16x512
-//      outputs (deterministic order), writing the normalised output.
+//  full_attention_page           the reference's one-page-per-call API: 8 chunks per page,
+//      the last chunk merges them into the running max/sum/out state (out unnormalised, bf16).
+//  full_attention_paged / the decode workspace's full layers: every row of a layer in one
+//      split-KV pass on the tensor cores (mma.sync, 16 q heads = the MMA's 16 rows), then a
+//      merge kernel; the row count may live in device memory so CUDA-graph replays follow
+//      the position.
 #include <math_constants.h>
 
 #include "g4_internal.h"
@@ -155,46 +157,6 @@ __device__ __forceinline__ void load_q(const uint16_t* q, float* qs) {
   __syncthreads();
 }
 
-// ---------------------------------------------------------------------------- sliding
-__global__ void __launch_bounds__(kAttnThreads) sliding_attention_kernel(const uint16_t* __restrict__ q,
-                                                                         const uint16_t* __restrict__ k,
-                                                                         const uint16_t* __restrict__ v,
-                                                                         const float* __restrict__ mask, int nkv,
-                                                                         uint16_t* __restrict__ out, float* part,
-                                                                         Scratch* scr) {
-  constexpr int D = DS, NQ = GS, P = 2 * NQ + NQ * D;
-  constexpr int S = TS / kChunk;
-  __shared__ float qs[NQ * D];
-  __shared__ int last;
-  const int h = blockIdx.x / S, c = blockIdx.x % S;
-  load_q<D, NQ>(q + h * NQ * D, qs);
-  RowSrc src;
-  src.k = k + (static_cast<long long>(c) * kChunk * nkv + h) * D;
-  src.v = v + (static_cast<long long>(c) * kChunk * nkv + h) * D;
-  src.stride = static_cast<long long>(nkv) * D;
-  src.mask = mask + c * kChunk;
-  src.nvalid = kChunk;
-  float* mine = part + (h * S + c) * P;
-  attend_chunk<D, NQ>(qs, src, mine);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    last = (atom_add_acq_rel_gpu(&scr->attn_count[h], 1u) == S - 1);
-  }
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  const float* ph = part + h * S * P;
-  for (int o = threadIdx.x; o < NQ * D; o += kAttnThreads) {
-    const int hh = o / D, d = o % D;
-    float M, Ls;
-    merge_stats<D, NQ>(ph, S, hh, M, Ls);
-    const float val = merge_out<D, NQ>(ph, S, hh, d, M);
-    out[h * NQ * D + o] = f32_to_bf16(Ls > 0.f ? val / Ls : 0.f);
-  }
-  if (threadIdx.x == 0) scr->attn_count[h] = 0u;
-}
-
 // ---------------------------------------------------------------------------- per page
 __global__ void __launch_bounds__(kAttnThreads) full_page_kernel(const uint16_t* __restrict__ q,
                                                                  const uint16_t* __restrict__ k,
@@ -251,78 +213,380 @@ __global__ void __launch_bounds__(kAttnThreads) full_page_kernel(const uint16_t*
   if (threadIdx.x == 0) scr->attn_count[63] = 0u;
 }
 
-// ---------------------------------------------------------------------------- all pages
-__global__ void __launch_bounds__(kAttnThreads) full_paged_kernel(const uint16_t* __restrict__ q,
-                                                                  const uint16_t* const* __restrict__ k_pages,
-                                                                  const uint16_t* const* __restrict__ v_pages,
-                                                                  int n_pages, int last_row, int nq,
-                                                                  float* running_sum, uint16_t* out, float* part,
-                                                                  Scratch* scr, uint64_t budget_ns) {
-  constexpr int D = DF, NQ = GF, P = 2 * NQ + NQ * D;
-  constexpr int CPP = TF / kChunk;  // chunks per page
-  __shared__ float qs[NQ * D];
-  __shared__ int fail;
-  const uint64_t deadline = global_ns() + budget_ns;
-  for (int i = threadIdx.x; i < NQ * D; i += kAttnThreads) qs[i] = (i < nq * D) ? bf16_to_f32(q[i]) : 0.f;
-  __syncthreads();
-  const int nchunks = (n_pages - 1) * CPP + (last_row / kChunk) + 1;
-  for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
-    const int p = c / CPP, r0 = (c % CPP) * kChunk;
-    RowSrc src;
-    src.k = k_pages[p] + static_cast<long long>(r0) * D;
-    src.v = v_pages[p] + static_cast<long long>(r0) * D;
-    src.stride = D;
-    src.mask = nullptr;
-    src.nvalid = (p == n_pages - 1) ? min(kChunk, last_row + 1 - r0) : kChunk;
-    attend_chunk<D, NQ>(qs, src, part + c * P);
-    __syncthreads();
+// ---------------------------------------------------------------------------- sliding
+// One CTA per (kv head, 64-slot chunk): warp w owns slots w*8..w*8+7 of the chunk, lane
+// l dims 8l..8l+7.  Every K and V row of a valid slot is loaded with one 16-byte load per
+// lane, all issued before any arithmetic; slots whose mask is 0 are not read.  Scores in
+// f32 (products of bf16 values are exact), softmax with the chunk's max, then the last
+// chunk of a head merges the 16 partials in chunk order.
+constexpr int kSaThreads = 256;
+constexpr int kSaRows = 64;
+constexpr int kSaPart = 2 * GS + GS * DS;  // m[GS], l[GS], o[GS][DS]
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4 w, float (&f)[8]) {
+  const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = bf16_to_f32(static_cast<uint16_t>(ww[i] & 0xFFFFu));
+    f[2 * i + 1] = bf16_to_f32(static_cast<uint16_t>(ww[i] >> 16));
   }
-  // bounded grid-wide wait
-  if (threadIdx.x == 0) {
-    __threadfence();
-    atom_add_release_gpu(&scr->attn_done, 1u);
-    uint32_t spins = 0;
-    fail = 0;
-    while (ld_acquire_gpu(&scr->attn_done) < gridDim.x) {
-      if ((++spins & 63u) == 0u && global_ns() > deadline) {
-        fail = 1;
-        atomicOr(&scr->status, DEV_ERR_TIMEOUT_GRID);
-        break;
+}
+
+__global__ void __launch_bounds__(kSaThreads) sliding_attn_kernel(const uint16_t* q, const uint16_t* k,
+                                                                  const uint16_t* v, const float* mask, int nkv,
+                                                                  int nchunks, uint16_t* out, float* part,
+                                                                  Scratch* scr) {
+  __shared__ float s[GS][kSaRows];
+  __shared__ __align__(16) float red[kSaThreads / 32][GS][DS];
+  __shared__ float mh[GS], lh[GS];
+  __shared__ int last;
+  const int h = blockIdx.x / nchunks, c = blockIdx.x % nchunks;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  pdl_wait();  // q, the caches and the mask come from earlier kernels
+  const int rbase = c * kSaRows + warp * 8;
+  const float mv = lane < 8 ? mask[rbase + lane] : 0.f;
+  const uint32_t valid = __ballot_sync(0xffffffffu, mv > 0.f) & 0xFFu;
+  const uint16_t* qh = q + static_cast<size_t>(h) * GS * DS + lane * 8;
+  const uint4 q0 = *reinterpret_cast<const uint4*>(qh);
+  const uint4 q1 = *reinterpret_cast<const uint4*>(qh + DS);
+  uint4 kk[8], vv[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    kk[j] = make_uint4(0u, 0u, 0u, 0u);
+    vv[j] = kk[j];
+    if ((valid >> j) & 1u) {
+      const size_t off = (static_cast<size_t>(rbase + j) * nkv + h) * DS + lane * 8;
+      kk[j] = *reinterpret_cast<const uint4*>(k + off);
+      vv[j] = *reinterpret_cast<const uint4*>(v + off);
+    }
+  }
+  pdl_launch_dependents();
+  float qa[8], qb[8];
+  bf16x8_to_f32(q0, qa);
+  bf16x8_to_f32(q1, qb);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float kf[8];
+    bf16x8_to_f32(kk[j], kf);
+    float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      d0 = fmaf(qa[i], kf[i], d0);
+      d1 = fmaf(qb[i], kf[i], d1);
+    }
+    d0 = warp_sum(d0);
+    d1 = warp_sum(d1);
+    if (lane == 0) {
+      const bool ok = (valid >> j) & 1u;
+      s[0][warp * 8 + j] = ok ? d0 : -CUDART_INF_F;
+      s[1][warp * 8 + j] = ok ? d1 : -CUDART_INF_F;
+    }
+  }
+  __syncthreads();
+  if (warp < GS) {
+    const float a = s[warp][lane], b = s[warp][lane + 32];
+    const float m = warp_max(fmaxf(a, b));
+    const float ea = (a == -CUDART_INF_F) ? 0.f : expf(a - m);
+    const float eb = (b == -CUDART_INF_F) ? 0.f : expf(b - m);
+    const float l = warp_sum(ea + eb);
+    s[warp][lane] = ea;
+    s[warp][lane + 32] = eb;
+    if (lane == 0) {
+      mh[warp] = m;
+      lh[warp] = l;
+    }
+  }
+  __syncthreads();
+  float o0[8], o1[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o0[i] = o1[i] = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if ((valid >> j) & 1u) {
+      float vf[8];
+      bf16x8_to_f32(vv[j], vf);
+      const float p0 = s[0][warp * 8 + j], p1 = s[1][warp * 8 + j];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        o0[i] = fmaf(p0, vf[i], o0[i]);
+        o1[i] = fmaf(p1, vf[i], o1[i]);
       }
     }
   }
+  float4* r0 = reinterpret_cast<float4*>(&red[warp][0][lane * 8]);
+  float4* r1 = reinterpret_cast<float4*>(&red[warp][1][lane * 8]);
+  r0[0] = make_float4(o0[0], o0[1], o0[2], o0[3]);
+  r0[1] = make_float4(o0[4], o0[5], o0[6], o0[7]);
+  r1[0] = make_float4(o1[0], o1[1], o1[2], o1[3]);
+  r1[1] = make_float4(o1[4], o1[5], o1[6], o1[7]);
   __syncthreads();
-  if (!fail) {
+  float* mine = part + static_cast<size_t>(h * nchunks + c) * kSaPart;
+  for (int o = tid; o < GS * DS; o += kSaThreads) {
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kSaThreads / 32; ++w) acc += red[w][o / DS][o % DS];
+    mine[2 * GS + o] = acc;
+  }
+  if (tid < GS) {
+    mine[tid] = mh[tid];
+    mine[GS + tid] = lh[tid];
+  }
+  __syncthreads();
+  if (tid == 0) {
     __threadfence();
-    for (int o = blockIdx.x * kAttnThreads + threadIdx.x; o < nq * D; o += gridDim.x * kAttnThreads) {
-      const int h = o / D, d = o % D;
-      float M, Ls;
-      merge_stats<D, NQ>(part, nchunks, h, M, Ls);
-      const float val = merge_out<D, NQ>(part, nchunks, h, d, M);
-      out[o] = f32_to_bf16(Ls > 0.f ? val / Ls : 0.f);
-      if (d == 0) running_sum[h] = 1.0f;
-    }
+    last = (atom_add_acq_rel_gpu(&scr->attn_count[h], 1u) == static_cast<uint32_t>(nchunks) - 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    // the last CTA to leave resets both counters (every CTA has passed the wait)
-    if (atom_add_acq_rel_gpu(&scr->attn_count[62], 1u) == gridDim.x - 1) {
-      scr->attn_done = 0u;
-      scr->attn_count[62] = 0u;
-      __threadfence();
+  if (!last) return;
+  __threadfence();
+  const float* ph = part + static_cast<size_t>(h) * nchunks * kSaPart;
+  for (int o = tid; o < GS * DS; o += kSaThreads) {
+    const int hh = o / DS;
+    float M = -CUDART_INF_F;
+    for (int cc = 0; cc < nchunks; ++cc) M = fmaxf(M, __ldcg(ph + cc * kSaPart + hh));
+    float Ls = 0.f, acc = 0.f;
+    if (M != -CUDART_INF_F) {
+      for (int cc = 0; cc < nchunks; ++cc) {
+        const float m = __ldcg(ph + cc * kSaPart + hh);
+        if (m == -CUDART_INF_F) continue;
+        const float w = expf(m - M);
+        Ls += __ldcg(ph + cc * kSaPart + GS + hh) * w;
+        acc += __ldcg(ph + cc * kSaPart + 2 * GS + o) * w;
+      }
     }
+    out[static_cast<size_t>(h) * GS * DS + o] = f32_to_bf16(Ls > 0.f ? acc / Ls : 0.f);
   }
+  if (tid == 0) scr->attn_count[h] = 0u;
+}
+
+// ---------------------------------------------------------------------------- full (MQA)
+// Split-KV over rows [0, n) of the single K/V head: the rows are cut into one contiguous
+// range per CTA (a multiple of 8 rows), each range runs in tiles of 32 rows staged in
+// shared memory with cp.async (16-byte chunks XOR-swizzled by row, so ldmatrix reads are
+// conflict-free), S = Q K^T and O += P V on the tensor cores (mma.sync m16n8k16, bf16
+// operands, f32 accumulators; the 16 q heads are the M = 16 rows), online softmax across
+// the CTA's tiles.  P enters the MMA as bf16 hi + lo parts, so the weights keep ~16
+// mantissa bits.  A second kernel (programmatic dependent launch: it waits for the first
+// to complete) merges the per-CTA partials in CTA order and writes the normalised output.
+constexpr int kFaThreads = 128;
+constexpr int kFaTile = 32;
+constexpr int kFaQStride = DF * 2 + 16;          // padded Q row in shared memory (bytes)
+constexpr int kFaPart = 2 * GF + GF * DF;        // m[16], l[16], o[16][512]
+constexpr int kFaMaxCtas = 512;
+
+struct FaSmem {
+  uint8_t k[kFaTile * DF * 2];
+  uint8_t v[kFaTile * DF * 2];
+  uint8_t q[GF * kFaQStride];
+  float s[GF][kFaTile + 1];
+  float m[GF], l[GF], alpha[GF];
+};
+
+// Where the K/V rows live: a page table of [TF, DF] pages (the reference's page cache)
+// or one contiguous [rows, DF] array (the decode workspace); the row count from the host
+// or from a device int32 (graph replays), clamped to `max_rows` either way.
+struct FaSrc {
+  const uint16_t* const* k_pages;
+  const uint16_t* const* v_pages;
+  const uint16_t* k;
+  const uint16_t* v;
+  const int32_t* n_dev;
+  int n_host;
+  int max_rows;
+};
+
+__device__ __forceinline__ const uint16_t* fa_row(const FaSrc& s, bool is_v, int r) {
+  if (s.k_pages != nullptr)
+    return (is_v ? s.v_pages : s.k_pages)[r / TF] + static_cast<size_t>(r % TF) * DF;
+  return (is_v ? s.v : s.k) + static_cast<size_t>(r) * DF;
+}
+
+// Rows, rows per CTA and active CTAs: the same on both kernels.
+__device__ __forceinline__ void fa_split(const FaSrc& s, int grid, int& n, int& rpc, int& nact) {
+  n = s.n_dev != nullptr ? *s.n_dev : s.n_host;
+  n = max(0, min(n, s.max_rows));
+  rpc = (n + grid - 1) / grid;
+  rpc = max(8, (rpc + 7) & ~7);
+  nact = (n + rpc - 1) / rpc;
+}
+
+__global__ void __launch_bounds__(kFaThreads) fa_partial_kernel(const uint16_t* q, int nq, FaSrc src,
+                                                                float* part) {
+  extern __shared__ __align__(128) uint8_t fa_raw[];
+  FaSmem& sm = *reinterpret_cast<FaSmem*>(fa_raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  pdl_wait();  // q and the newest K/V row come from the projection kernel
+  int n, rpc, nact;
+  fa_split(src, gridDim.x, n, rpc, nact);
+  const int r0 = blockIdx.x * rpc, r1 = min(n, r0 + rpc);
+  if (r0 >= r1) {
+    pdl_launch_dependents();
+    return;
+  }
+  const uint32_t qb = smem_u32(sm.q), kb = smem_u32(sm.k), vb = smem_u32(sm.v);
+  for (int i = tid; i < GF * (DF / 8); i += kFaThreads) {
+    const int hh = i / (DF / 8), c = i % (DF / 8);
+    const bool ok = hh < nq;
+    cp_async16(qb + hh * kFaQStride + c * 16, ok ? q + hh * DF + c * 8 : q, ok ? 16u : 0u);
+  }
+  if (tid < GF) {
+    sm.m[tid] = -CUDART_INF_F;
+    sm.l[tid] = 0.f;
+  }
+  float acc[16][4];
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+
+  for (int tr = r0; tr < r1; tr += kFaTile) {
+    for (int i = tid; i < kFaTile * (DF / 8); i += kFaThreads) {
+      const int rr = i / (DF / 8), c = i % (DF / 8);
+      const int r = tr + rr;
+      const bool ok = r < r1;
+      const uint32_t off = rr * (DF * 2) + ((c ^ (rr & 7)) * 16);
+      cp_async16(kb + off, ok ? fa_row(src, false, r) + c * 8 : q, ok ? 16u : 0u);
+      cp_async16(vb + off, ok ? fa_row(src, true, r) + c * 8 : q, ok ? 16u : 0u);
+    }
+    if (tr == r0) pdl_launch_dependents();
+    cp_async_wait_all();
+    __syncthreads();
+    // S[16 heads][8 rows of this warp] = Q K^T over the 512 dims
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int j = 0; j < DF / 16; j += 2) {
+      uint32_t b0, b1, b2, b3;
+      {
+        const int row = 8 * warp + (lane & 7), chunk = 2 * j + (lane >> 3);
+        ldsm_x4(kb + row * (DF * 2) + ((chunk ^ (row & 7)) * 16), b0, b1, b2, b3);
+      }
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        uint32_t a0, a1, a2, a3;
+        const int qrow = (lane & 7) + 8 * ((lane >> 3) & 1), qcol = (j + jj) * 16 + 8 * (lane >> 4);
+        ldsm_x4(qb + qrow * kFaQStride + qcol * 2, a0, a1, a2, a3);
+        mma_bf16(sc, a0, a1, a2, a3, jj ? b2 : b0, jj ? b3 : b1);
+      }
+    }
+    {
+      const int rr = 8 * warp + 2 * t;
+      const bool v0 = tr + rr < r1, v1 = tr + rr + 1 < r1;
+      sm.s[g][rr] = v0 ? sc[0] : -CUDART_INF_F;
+      sm.s[g][rr + 1] = v1 ? sc[1] : -CUDART_INF_F;
+      sm.s[g + 8][rr] = v0 ? sc[2] : -CUDART_INF_F;
+      sm.s[g + 8][rr + 1] = v1 ? sc[3] : -CUDART_INF_F;
+    }
+    __syncthreads();
+    // online softmax: warp w updates heads 4w..4w+3, lane = tile row
+#pragma unroll
+    for (int hh = 0; hh < 4; ++hh) {
+      const int h = 4 * warp + hh;
+      const float sv = sm.s[h][lane];
+      const float mold = sm.m[h];
+      const float mnew = fmaxf(mold, warp_max(sv));
+      const float p = (sv == -CUDART_INF_F) ? 0.f : expf(sv - mnew);
+      const float ls = warp_sum(p);
+      sm.s[h][lane] = p;
+      if (lane == 0) {
+        const float a = (mold == -CUDART_INF_F) ? 0.f : expf(mold - mnew);
+        sm.alpha[h] = a;
+        sm.l[h] = sm.l[h] * a + ls;
+        sm.m[h] = mnew;
+      }
+    }
+    __syncthreads();
+    // O[16 heads][128 dims of this warp] = O * alpha + P V
+    const float al = sm.alpha[g], ah = sm.alpha[g + 8];
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      acc[nt][0] *= al;
+      acc[nt][1] *= al;
+      acc[nt][2] *= ah;
+      acc[nt][3] *= ah;
+    }
+#pragma unroll
+    for (int j = 0; j < kFaTile / 16; ++j) {
+      const int c0 = 16 * j + 2 * t;
+      const float p[8] = {sm.s[g][c0], sm.s[g][c0 + 1], sm.s[g + 8][c0], sm.s[g + 8][c0 + 1],
+                          sm.s[g][c0 + 8], sm.s[g][c0 + 9], sm.s[g + 8][c0 + 8], sm.s[g + 8][c0 + 9]};
+      uint32_t hi[4], lo[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float x0 = round_bf16(p[2 * i]), x1 = round_bf16(p[2 * i + 1]);
+        hi[i] = pack_bf16x2(x0, x1);
+        lo[i] = pack_bf16x2(p[2 * i] - x0, p[2 * i + 1] - x1);
+      }
+#pragma unroll
+      for (int nt = 0; nt < 16; nt += 2) {
+        uint32_t b0, b1, b2, b3;
+        const int vrow = 16 * j + (lane & 7) + 8 * ((lane >> 3) & 1), chunk = 16 * warp + nt + (lane >> 4);
+        ldsm_x4_trans(vb + vrow * (DF * 2) + ((chunk ^ (vrow & 7)) * 16), b0, b1, b2, b3);
+        mma_bf16(acc[nt], hi[0], hi[1], hi[2], hi[3], b0, b1);
+        mma_bf16(acc[nt], lo[0], lo[1], lo[2], lo[3], b0, b1);
+        mma_bf16(acc[nt + 1], hi[0], hi[1], hi[2], hi[3], b2, b3);
+        mma_bf16(acc[nt + 1], lo[0], lo[1], lo[2], lo[3], b2, b3);
+      }
+    }
+    __syncthreads();  // the next tile overwrites K, V and S
+  }
+  float* mine = part + static_cast<size_t>(blockIdx.x) * kFaPart;
+  if (tid < GF) {
+    mine[tid] = sm.m[tid];
+    mine[GF + tid] = sm.l[tid];
+  }
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt) {
+    const int d = 128 * warp + 8 * nt + 2 * t;
+    *reinterpret_cast<float2*>(mine + 2 * GF + g * DF + d) = make_float2(acc[nt][0], acc[nt][1]);
+    *reinterpret_cast<float2*>(mine + 2 * GF + (g + 8) * DF + d) = make_float2(acc[nt][2], acc[nt][3]);
+  }
+}
+
+// Two CTAs per head, 256 dims each: merge weights of the active partials in CTA order.
+__global__ void __launch_bounds__(256) fa_merge_kernel(const float* part, FaSrc src, int grid, float* running_sum,
+                                                       uint16_t* out) {
+  __shared__ float w[kFaMaxCtas];
+  __shared__ float red[8];
+  __shared__ float Mall, Lall;
+  const int h = blockIdx.x >> 1, half = blockIdx.x & 1, tid = threadIdx.x;
+  pdl_wait();  // every partial of the previous kernel is written
+  int n, rpc, nact;
+  fa_split(src, grid, n, rpc, nact);
+  float m = -CUDART_INF_F;
+  for (int p = tid; p < nact; p += 256) m = fmaxf(m, __ldcg(part + static_cast<size_t>(p) * kFaPart + h));
+  m = warp_max(m);
+  if ((tid & 31) == 0) red[tid >> 5] = m;
+  __syncthreads();
+  if (tid == 0) {
+    float x = red[0];
+    for (int i = 1; i < 8; ++i) x = fmaxf(x, red[i]);
+    Mall = x;
+  }
+  __syncthreads();
+  const float M = Mall;
+  float l = 0.f;
+  for (int p = tid; p < nact; p += 256) {
+    const float mp = __ldcg(part + static_cast<size_t>(p) * kFaPart + h);
+    const float wp = (mp == -CUDART_INF_F || M == -CUDART_INF_F) ? 0.f : expf(mp - M);
+    w[p] = wp;
+    l += wp * __ldcg(part + static_cast<size_t>(p) * kFaPart + GF + h);
+  }
+  l = warp_sum(l);
+  __syncthreads();
+  if ((tid & 31) == 0) red[tid >> 5] = l;
+  __syncthreads();
+  if (tid == 0) {
+    float x = 0.f;
+    for (int i = 0; i < 8; ++i) x += red[i];
+    Lall = x;
+  }
+  __syncthreads();
+  const int d = half * 256 + tid;
+  float o = 0.f;
+  for (int p = 0; p < nact; ++p) o += w[p] * __ldcg(part + static_cast<size_t>(p) * kFaPart + 2 * GF + h * DF + d);
+  out[h * DF + d] = f32_to_bf16(Lall > 0.f ? o / Lall : 0.f);
+  if (half == 0 && tid == 0) running_sum[h] = 1.0f;
 }
 
 // ---------------------------------------------------------------------------- launchers
-g4_status launch_sliding_attention(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
-                                   const float* mask, uint16_t* out) {
-  const int nkv = NS / ctx->tp_world;
-  sliding_attention_kernel<<<nkv * (TS / kChunk), kAttnThreads, 0, ctx->stream>>>(q, k, v, mask, nkv, out,
-                                                                                  ctx->buf.attn, ctx->buf.scratch);
-  return check_cuda(ctx, cudaGetLastError(), "sliding_attention");
-}
-
 g4_status launch_full_page(g4_ctx* ctx, bool first, const uint16_t* q, const uint16_t* k, const uint16_t* v,
                            const float* mask, float* rmax, float* rsum, uint16_t* out) {
   const int nq = GF / ctx->tp_world;
@@ -331,20 +595,70 @@ g4_status launch_full_page(g4_ctx* ctx, bool first, const uint16_t* q, const uin
   return check_cuda(ctx, cudaGetLastError(), "full_attention_page");
 }
 
-g4_status launch_full_paged(g4_ctx* ctx, const uint16_t* q, const uint16_t* const* kp, const uint16_t* const* vp,
-                            int n_pages, int last_row, float* rsum, uint16_t* out) {
-  const int nq = GF / ctx->tp_world;
-  const int nchunks = (n_pages - 1) * (TF / kChunk) + last_row / kChunk + 1;
-  int grid = nchunks < ctx->sm_count ? nchunks : ctx->sm_count;
-  uint64_t budget = ctx->wait_budget_ns;
+}  // namespace g4
+
+namespace g4 {
+
+// GQA attention over `rows` cache rows of the sliding layout [rows, Ns/N, Ds] (rows a
+// multiple of 64): the reference's sliding_attention at rows = Ts, and the same geometry
+// over a longer cache (BASELINE config 3's 8 KV heads of 256 at 8192 positions).
+g4_status launch_gqa_attention(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                               const float* mask, int rows, uint16_t* out) {
+  static_assert(static_cast<size_t>(NS) * (E / kSaRows) * kSaPart <= kAttnFloats, "partials fit");
+  int nkv = NS / ctx->tp_world, nchunks = rows / kSaRows;
   float* part = ctx->buf.attn;
   Scratch* scr = ctx->buf.scratch;
-  void* args[] = {(void*)&q, (void*)&kp, (void*)&vp, (void*)&n_pages, (void*)&last_row, (void*)&nq,
-                  (void*)&rsum, (void*)&out, (void*)&part, (void*)&scr, (void*)&budget};
-  return check_cuda(ctx,
-                    cudaLaunchCooperativeKernel((const void*)full_paged_kernel, dim3(grid), dim3(kAttnThreads), args,
-                                                0, ctx->stream),
-                    "full_attention_paged");
+  void* args[] = {(void*)&q, (void*)&k, (void*)&v, (void*)&mask, (void*)&nkv, (void*)&nchunks, (void*)&out,
+                  (void*)&part, (void*)&scr};
+  return launch_kernel(ctx, (const void*)sliding_attn_kernel, dim3(nkv * nchunks), dim3(kSaThreads), 0, args,
+                       false, "gqa attention");
+}
+
+g4_status launch_sliding_attention(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                   const float* mask, uint16_t* out) {
+  return launch_gqa_attention(ctx, q, k, v, mask, TS, out);
+}
+
+// Full (MQA) attention over rows [0, n) of `src`; grid sized for src.max_rows.
+static g4_status launch_full_attention(g4_ctx* ctx, const uint16_t* q, const FaSrc& src, float* rsum,
+                                       uint16_t* out) {
+  static_assert(static_cast<size_t>(kFaMaxCtas) * kFaPart <= kAttnFloats, "partials fit the attention scratch");
+  int nq = GF / ctx->tp_world;
+  const int want = (src.max_rows + 7) / 8;
+  int grid = 2 * ctx->sm_count;
+  if (grid > kFaMaxCtas) grid = kFaMaxCtas;
+  if (want < grid) grid = want < 1 ? 1 : want;
+  g4_status st = allow_max_dynamic_smem(ctx, (const void*)fa_partial_kernel, sizeof(FaSmem), "full attention");
+  if (st != G4_OK) return st;
+  float* part = ctx->buf.attn;
+  FaSrc s = src;
+  void* a1[] = {(void*)&q, (void*)&nq, (void*)&s, (void*)&part};
+  st = launch_kernel(ctx, (const void*)fa_partial_kernel, dim3(grid), dim3(kFaThreads), sizeof(FaSmem), a1, false,
+                     "full attention partials");
+  if (st != G4_OK) return st;
+  void* a2[] = {(void*)&part, (void*)&s, (void*)&grid, (void*)&rsum, (void*)&out};
+  return launch_kernel(ctx, (const void*)fa_merge_kernel, dim3(2 * nq), dim3(256), 0, a2, false,
+                       "full attention merge");
+}
+
+g4_status launch_full_paged(g4_ctx* ctx, const uint16_t* q, const uint16_t* const* kp, const uint16_t* const* vp,
+                            int n_pages, int last_row, float* rsum, uint16_t* out) {
+  FaSrc s = {};
+  s.k_pages = kp;
+  s.v_pages = vp;
+  s.n_host = (n_pages - 1) * TF + last_row + 1;
+  s.max_rows = s.n_host;
+  return launch_full_attention(ctx, q, s, rsum, out);
+}
+
+g4_status launch_full_rows(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                           const int32_t* n_rows, int max_rows, float* rsum, uint16_t* out) {
+  FaSrc s = {};
+  s.k = k;
+  s.v = v;
+  s.n_dev = n_rows;
+  s.max_rows = max_rows;
+  return launch_full_attention(ctx, q, s, rsum, out);
 }
 
 }  // namespace g4

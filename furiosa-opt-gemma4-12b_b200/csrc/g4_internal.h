@@ -5,6 +5,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <vector>
 
 #include "g4.h"
 
@@ -101,6 +102,10 @@ g4_status launch_decoder_feedforward(g4_ctx* ctx, uint16_t* residual, const uint
                                      const float* up_gs, const float* gate_gs, const float* down_gs,
                                      const uint16_t* post_w, const uint16_t* layer_scalar);
 g4_status allreduce_f32(g4_ctx* ctx, float* buf, size_t count);
+// Hands device buffers a loader allocated for `model` to it: freed by g4_model_destroy.
+void model_adopt(g4_model* model, const std::vector<void*>& ptrs, int device);
+// Every rank's one 64-bit word into out[world] (NCCL all-gather on the context's stream).
+g4_status allgather_u64(g4_ctx* ctx, const uint64_t* in, uint64_t* out);
 bool mlp_tc_enabled(const g4_ctx* ctx);
 g4_status launch_decoder_feedforward_tc(g4_ctx* ctx, uint16_t* residual, const uint16_t* pre_w,
                                         const uint8_t* up_p, const uint8_t* gate_p, const uint8_t* down_p,

@@ -14,6 +14,9 @@
 //  LmHeadOp: final_norm_and_logits (src/ops.rs:255-312, src/device/shared/lm_head.rs):
 //            stage RMSNorm(x) as bf16; items = 8 vocab rows x both K halves; epilogue
 //            bf16 logit -> bf16(tanh(l/30)*30).
+#include <cstdlib>
+#include <cstring>
+
 #include "g4_internal.h"
 #include "g4_stream.cuh"
 
@@ -452,11 +455,31 @@ static g4_status launch_stream(g4_ctx* ctx, const Op& op, uint32_t slot_bytes, u
 }
 
 // ---------------------------------------------------------------------------- launchers
+g4_status launch_qkv_fp8(g4_ctx*, bool, const uint16_t*, const uint8_t* const[3], const uint16_t* const[3],
+                         const uint16_t*, const uint16_t*, const uint16_t*, const int32_t*, const int32_t*,
+                         const uint16_t*, const uint16_t*, uint16_t*, uint16_t*, uint16_t*, long long);
+g4_status launch_oproj_fp8(g4_ctx*, bool, const uint16_t*, const float*, const uint16_t*, const uint8_t*,
+                           const uint16_t*, uint16_t*);
+
+// FP8 projections on one GPU run on the tensor-core GEMV of g4_fp8.cu unless
+// G4B200_PROJ_KERNEL=stream asks for the streaming engine (which also serves NVFP4 weights
+// and tensor-parallel contexts).
+static bool fp8_tensor_path(const g4_ctx* ctx) {
+  static const bool stream = [] {
+    const char* e = std::getenv("G4B200_PROJ_KERNEL");
+    return e != nullptr && std::strcmp(e, "stream") == 0;
+  }();
+  return !stream && ctx->tp_world == 1;
+}
+
 g4_status launch_qkv(g4_ctx* ctx, bool full, bool nvfp4, const uint16_t* x, const uint8_t* const w[3],
                      const uint8_t* const bs[3], const uint16_t* const rs[3], const float* const gs[3],
                      const uint16_t* in_w, const uint16_t* qn_w, const uint16_t* kn_w, const int32_t* kv_off,
                      const int32_t* rope_off, const uint16_t* cosT, const uint16_t* sinT, uint16_t* kcache,
-                     uint16_t* vcache, uint16_t* q_out) {
+                     uint16_t* vcache, uint16_t* q_out, long long cache_elems) {
+  if (!nvfp4 && fp8_tensor_path(ctx))
+    return launch_qkv_fp8(ctx, full, x, w, rs, in_w, qn_w, kn_w, kv_off, rope_off, cosT, sinT, kcache, vcache, q_out,
+                          cache_elems);
   QkvOp op;
   const int tp = ctx->tp_world;
   op.D = full ? DF : DS;
@@ -481,7 +504,10 @@ g4_status launch_qkv(g4_ctx* ctx, bool full, bool nvfp4, const uint16_t* x, cons
   op.table_elems = static_cast<long long>(E) * op.D;
   op.kc = kcache;
   op.vc = vcache;
-  op.cache_elems = full ? static_cast<long long>(TF) * DF : static_cast<long long>(TS) * op.nk * DS;
+  // the reference's cache tensors (one page of a full layer, the whole sliding ring)
+  // unless the caller passes a larger contiguous cache (the decode workspace)
+  op.cache_elems = cache_elems > 0 ? cache_elems
+                                   : (full ? static_cast<long long>(TF) * DF : static_cast<long long>(TS) * op.nk * DS);
   op.q_out = q_out;
   op.scr = ctx->buf.scratch;
   op.rows = ctx->buf.rows;
@@ -501,6 +527,7 @@ g4_status launch_qkv(g4_ctx* ctx, bool full, bool nvfp4, const uint16_t* x, cons
 g4_status launch_oproj(g4_ctx* ctx, bool full, bool nvfp4, const uint16_t* x, const float* rsum, const uint16_t* post_w,
                        const uint8_t* w, const uint8_t* bs, const uint16_t* row_scale, const float* gsc,
                        uint16_t* residual) {
+  if (!nvfp4 && fp8_tensor_path(ctx)) return launch_oproj_fp8(ctx, full, x, rsum, post_w, w, row_scale, residual);
   OprojOp op;
   const int tp = ctx->tp_world;
   op.K = (full ? QF : QS) / tp;

@@ -25,7 +25,8 @@ __all__ = [
     "full_attention_page", "full_attention_output", "decoder_feedforward",
     "final_norm_and_logits", "full_attention_paged", "argmax_bf16", "dequant_nvfp4",
     "dequant_fp8", "sliding_project_qkv_nvfp4", "sliding_attention_output_nvfp4",
-    "decoder_feedforward_noalloc", "NOALLOC_MAX_INTERMEDIATE",
+    "decoder_feedforward_noalloc", "NOALLOC_MAX_INTERMEDIATE", "full_project_qkv_nvfp4",
+    "full_attention_output_nvfp4", "attention_gqa",
 ]
 
 H, L, W = 3840, 15360, 262144
@@ -223,10 +224,12 @@ for _n, _k in [("g4_embed_token", 3), ("g4_copy_hidden_state", 2), ("g4_sliding_
                ("g4_full_project_qkv", 15), ("g4_sliding_attention", 5), ("g4_sliding_attention_output", 5),
                ("g4_full_attention_first_page", 7), ("g4_full_attention_page", 7),
                ("g4_full_attention_output", 6), ("g4_decoder_feedforward", 13), ("g4_final_norm_and_logits", 4),
-               ("g4_sliding_project_qkv_nvfp4", 20), ("g4_sliding_attention_output_nvfp4", 6)]:
+               ("g4_sliding_project_qkv_nvfp4", 20), ("g4_sliding_attention_output_nvfp4", 6),
+               ("g4_full_project_qkv_nvfp4", 17), ("g4_full_attention_output_nvfp4", 7)]:
     _declare(_n, _k)
 LIB.g4_full_attention_paged.argtypes = [_vp, _vp, _vp, _vp, _i32, _i32, _vp, _vp]
 LIB.g4_argmax_bf16.argtypes = [_vp, _vp, _i32, _vp]
+LIB.g4_attention_gqa.argtypes = [_vp, _vp, _vp, _vp, _vp, _i32, _vp]
 LIB.g4_dequant_nvfp4.argtypes = [_vp, _vp, _vp, _i32, _i32, _vp]
 LIB.g4_dequant_fp8.argtypes = [_vp, _vp, _i64, _vp]
 LIB.g4_decoder_feedforward_noalloc.argtypes = [_vp, _u32] + [_vp] * 13
@@ -378,6 +381,61 @@ def sliding_attention_output_nvfp4(ctx: Context, x, post_attn_rms_weight, o_weig
     _expect("residual", residual, H, bf)
     ctx.call("g4_sliding_attention_output_nvfp4", x, post_attn_rms_weight, o_weight, o_block_scale,
              o_global_scale, residual)
+
+
+def full_project_qkv_nvfp4(ctx: Context, x, q_weight, k_weight, q_block_scale, k_block_scale, q_global_scale,
+                           k_global_scale, input_rms_weight, q_rms_weight, k_rms_weight, kv_offset, rope_offset, cos,
+                           sin, k_cache, v_cache, q_out):
+    """NVFP4 variant of full_project_qkv."""
+    t = _t()
+    n = ctx.world
+    u8, f8, bf, f32 = (t.uint8,), (t.uint8, t.float8_e4m3fn), (t.bfloat16,), (t.float32,)
+    _expect("x", x, H, bf)
+    _expect("q_weight", q_weight, QF // n * H // 2, u8)
+    _expect("k_weight", k_weight, PF * H // 2, u8)
+    _expect("q_block_scale", q_block_scale, QF // n * H // 16, f8)
+    _expect("k_block_scale", k_block_scale, PF * H // 16, f8)
+    _expect("q_global_scale", q_global_scale, 1, f32)
+    _expect("k_global_scale", k_global_scale, 1, f32)
+    _expect("cos", cos, E * DF, bf)
+    _expect("sin", sin, E * DF, bf)
+    _expect("k_cache", k_cache, TF * DF, bf)
+    _expect("v_cache", v_cache, TF * DF, bf)
+    _expect("q_out", q_out, GF // n * DF, bf)
+    ctx.call("g4_full_project_qkv_nvfp4", x, q_weight, k_weight, q_block_scale, k_block_scale, q_global_scale,
+             k_global_scale, input_rms_weight, q_rms_weight, k_rms_weight, kv_offset, rope_offset, cos, sin, k_cache,
+             v_cache, q_out)
+
+
+def full_attention_output_nvfp4(ctx: Context, x, running_sum, post_attn_rms_weight, o_weight, o_block_scale,
+                                o_global_scale, residual):
+    """NVFP4 variant of full_attention_output."""
+    t = _t()
+    n = ctx.world
+    bf = (t.bfloat16,)
+    _expect("x", x, GF // n * DF, bf)
+    _expect("running_sum", running_sum, GF // n, (t.float32,))
+    _expect("o_weight", o_weight, H * QF // n // 2, (t.uint8,))
+    _expect("o_block_scale", o_block_scale, H * QF // n // 16, (t.uint8, t.float8_e4m3fn))
+    _expect("o_global_scale", o_global_scale, 1, (t.float32,))
+    _expect("residual", residual, H, bf)
+    ctx.call("g4_full_attention_output_nvfp4", x, running_sum, post_attn_rms_weight, o_weight, o_block_scale,
+             o_global_scale, residual)
+
+
+def attention_gqa(ctx: Context, q, k, v, mask, out) -> None:
+    """GQA attention of the sliding geometry over mask.numel() cache rows."""
+    t = _t()
+    n = ctx.world
+    rows = mask.numel()
+    bf = (t.bfloat16,)
+    _expect("q", q, NS * GS // n * DS, bf)
+    _expect("k", k, rows * NS // n * DS, bf)
+    _expect("v", v, rows * NS // n * DS, bf)
+    _expect("mask", mask, rows, (t.float32,))
+    _expect("out", out, NS * GS // n * DS, bf)
+    ctx._check("g4_attention_gqa", LIB.g4_attention_gqa(ctx.handle, _ptr(q), _ptr(k), _ptr(v), _ptr(mask), rows,
+                                                        _ptr(out)))
 
 
 def _full_page(fn, ctx, q, k, v, mask, running_max, running_sum, out):

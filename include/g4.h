@@ -265,6 +265,113 @@ g4_status g4_sliding_attention_output_nvfp4(g4_ctx* ctx, const g4_bf16* x,
                                             const g4_f8e4m3* o_block_scale,
                                             const float* o_global_scale, g4_bf16* residual);
 
+/* NVFP4 variants of the full-attention (MQA) projections: as
+ * g4_full_project_qkv / g4_full_attention_output with each FP8 (weight, row scale) pair
+ * replaced by (packed E2M1 codes [N, K/2], E4M3 block scales [N, K/16], reciprocal f32
+ * global scale).  TP as the FP8 entry points. */
+g4_status g4_full_project_qkv_nvfp4(g4_ctx* ctx, const g4_bf16* x, const g4_f4x2* q_weight, const g4_f4x2* k_weight,
+                                    const g4_f8e4m3* q_block_scale, const g4_f8e4m3* k_block_scale,
+                                    const float* q_global_scale, const float* k_global_scale,
+                                    const g4_bf16* input_rms_weight, const g4_bf16* q_rms_weight,
+                                    const g4_bf16* k_rms_weight, const int32_t* kv_offset, const int32_t* rope_offset,
+                                    const g4_bf16* cos, const g4_bf16* sin, g4_bf16* k_cache, g4_bf16* v_cache,
+                                    g4_bf16* q_out);
+g4_status g4_full_attention_output_nvfp4(g4_ctx* ctx, const g4_bf16* x, const float* running_sum,
+                                         const g4_bf16* post_attn_rms_weight, const g4_f4x2* o_weight,
+                                         const g4_f8e4m3* o_block_scale, const float* o_global_scale,
+                                         g4_bf16* residual);
+
+/* GQA decode attention of the sliding geometry over a cache of any length (BASELINE
+ * config 3's synthetic 16 q heads over 8 KV heads of 256): q[Ns,Gs,Ds], k/v[n_rows,Ns,Ds],
+ * mask[n_rows] f32 (> 0 = attended), out[Ns,Gs,Ds]; n_rows a multiple of 64 up to 32768.
+ * g4_sliding_attention is this at n_rows = Ts.  TP: the rank's heads. */
+g4_status g4_attention_gqa(g4_ctx* ctx, const g4_bf16* q, const g4_bf16* k, const g4_bf16* v, const float* mask,
+                           int n_rows, g4_bf16* out);
+
+/* ------------------------------------------------------------------------------ */
+/* Decode runtime (src/host/load.rs Model, src/host/runtime.rs Workspace / Decode)  */
+/* ------------------------------------------------------------------------------ */
+
+/* The text decoder's weight set (MlpWeights / SlidingLayer / FullLayer / Model,
+ * src/host/load.rs:10-87) as device pointers registered by checkpoint tensor name:
+ *   model.language_model.embed_tokens.weight         bf16 [W, H] (tied lm_head; every rank
+ *                                                     holds the whole table)
+ *   model.language_model.norm.weight                 bf16 [H]
+ *   model.language_model.layers.<i>.<suffix>, suffix one of
+ *     input_layernorm.weight, post_attention_layernorm.weight,
+ *     pre_feedforward_layernorm.weight, post_feedforward_layernorm.weight   bf16 [H]
+ *     layer_scalar                                   bf16 [8] (the scalar replicated,
+ *                                                     load.rs:99-111)
+ *     self_attn.{q,k,v,o}_proj.weight                f8e4m3 [N, K] (no v_proj in full layers)
+ *     self_attn.{q,k,v,o}_proj.weight_scale          bf16 [N] per-row scale
+ *     self_attn.{q,k}_norm.weight                    bf16 [D]
+ *     mlp.{up,gate,down}_proj.weight_packed          u8 [N, K/2] E2M1 codes
+ *     mlp.{up,gate,down}_proj.weight_scale           f8e4m3 [N, K/16]
+ *     mlp.{up,gate,down}_proj.weight_global_scale    f32 [1], the RECIPROCAL of the
+ *                                                     checkpoint value (load.rs:171-191)
+ * Layer i is a full-attention layer iff i % 6 == 5 (load.rs:369-376).  Under tensor
+ * parallelism each tensor is the rank's shard as the per-op entry points take it.  The
+ * model only records pointers (it never frees them) unless a loader filled it.
+ * g4_model_create needs no GPU; sizes are checked by g4_workspace_create. */
+typedef struct g4_model g4_model;
+g4_status g4_model_create(int n_layers, g4_model** out);
+g4_status g4_model_destroy(g4_model* model);
+g4_status g4_model_set_tensor(g4_model* model, const char* name, const void* device_ptr, uint64_t bytes);
+const char* g4_model_last_error(const g4_model* model);
+/* load_model (src/host/load.rs:357-386) for the text decoder: memory-maps a safetensors
+ * checkpoint, checks every tensor's dtype and shape as the reference loader does
+ * (load.rs:89-191: BF16 norms and row scales [N, 1], F8_E4M3 projections, U8 NVFP4 codes
+ * [N, K/2], F8_E4M3 block scales [N, K/16], scalar F32 global scales that must be finite
+ * and non-zero), copies this context's tensor-parallel shard of each to the device (the
+ * global scale as its reciprocal, the layer scalar replicated to [8]) and returns a model
+ * that owns those buffers.  Errors name the tensor (g4_ctx_last_error). */
+g4_status g4_model_load_safetensors(g4_ctx* ctx, const char* path, int n_layers, g4_model** out);
+/* The same checks without a GPU: G4_OK if the file holds an n_layers text decoder that
+ * can be cut for `world` ranks; otherwise G4_ERR_BAD_ARG and the reason in msg. */
+g4_status g4_checkpoint_check(const char* path, int n_layers, int world, char* msg, uint64_t msg_len);
+/* 1 if layer `layer` is a full-attention layer (load.rs:369-376), else 0. */
+int g4_model_layer_is_full(int layer);
+
+/* Workspace (src/host/runtime.rs:135-211): RoPE tables (rope_data, :271-299), every
+ * layer's KV cache (sliding: ring [Ts, Ns/N, Ds]; full: [ceil(max_positions/512)*512, Df],
+ * i.e. the reference's 512-row pages back to back), the current mask row, the
+ * device-resident byte offsets (:213-228), the decode scratch of Decode (:301-309) and
+ * the logits [W/N].  Checks that every tensor of `model` is set with the shard size of
+ * the context's tensor-parallel world. */
+typedef struct g4_workspace g4_workspace;
+g4_status g4_workspace_create(g4_ctx* ctx, const g4_model* model, int max_positions, g4_workspace** out);
+g4_status g4_workspace_destroy(g4_workspace* ws);
+/* Device pointers of layer `layer`'s K and V caches and their size in bytes each. */
+g4_status g4_workspace_kv_cache(g4_workspace* ws, int layer, g4_bf16** k, g4_bf16** v, uint64_t* bytes);
+/* This rank's logits [W/N] of the last step and the hidden state x [H] (device). */
+g4_status g4_workspace_logits(g4_workspace* ws, const g4_bf16** logits, int* count);
+g4_status g4_workspace_hidden(g4_workspace* ws, const g4_bf16** x);
+
+/* Decode::run (src/host/runtime.rs:312-347): embed `token`, run every layer at position
+ * `pos` (writing that position's K/V), final norm and logits into the workspace, then the
+ * device argmax (g4_decode_last_prediction reads it).  Asynchronous on the context's
+ * stream. */
+g4_status g4_decode_run(g4_ctx* ctx, g4_workspace* ws, const g4_model* model, int32_t token, int32_t pos);
+/* Greedy decoding with the position and token kept on the device (replaces the host loop
+ * of src/host/generate.rs:194-298: prefill one position per step, read logits, sample):
+ *   g4_decode_begin  uploads prompt[prompt_len] for positions start_pos.. and resets the
+ *                    state; g4_decode_steps runs n steps (use_graph: one CUDA graph of the
+ *                    whole step, captured on first use, replayed per step; needs a
+ *                    non-default stream); each step's input is the next prompt token while
+ *                    the prompt lasts, then the previous step's argmax, which is recorded;
+ *   g4_decode_tokens synchronises and copies up to max_out recorded tokens to the host;
+ *   g4_generate_greedy runs prompt_len + max_new - 1 steps and returns max_new tokens. */
+g4_status g4_decode_begin(g4_ctx* ctx, g4_workspace* ws, const int32_t* prompt, int prompt_len, int start_pos,
+                          int max_new);
+g4_status g4_decode_steps(g4_ctx* ctx, g4_workspace* ws, const g4_model* model, int n_steps, int use_graph);
+g4_status g4_decode_tokens(g4_ctx* ctx, g4_workspace* ws, int32_t* out, int max_out, int* n_out);
+/* The greedy prediction of every step since g4_decode_begin (prompt positions included),
+ * in step order, up to max_out; and the last step's prediction with the next position. */
+g4_status g4_decode_predictions(g4_ctx* ctx, g4_workspace* ws, int32_t* out, int max_out, int* n_out);
+g4_status g4_decode_last_prediction(g4_ctx* ctx, g4_workspace* ws, int32_t* token, int32_t* next_pos);
+g4_status g4_generate_greedy(g4_ctx* ctx, g4_workspace* ws, const g4_model* model, const int32_t* prompt,
+                             int prompt_len, int start_pos, int max_new, int use_graph, int32_t* out_tokens);
+
 /* ------------------------------------------------------------------------------ */
 /* Allocation-free decoder_feedforward (no counterpart in the reference)            */
 /* ------------------------------------------------------------------------------ */
