@@ -222,6 +222,7 @@ __global__ void __launch_bounds__(kAttnThreads) full_page_kernel(const uint16_t*
 constexpr int kSaThreads = 256;
 constexpr int kSaRows = 64;
 constexpr int kSaPart = 2 * GS + GS * DS;  // m[GS], l[GS], o[GS][DS]
+constexpr int kMaxSaChunks = E / kSaRows;   // 512 chunks: a 32768-row cache
 
 __device__ __forceinline__ void bf16x8_to_f32(const uint4 w, float (&f)[8]) {
   const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
@@ -244,22 +245,20 @@ __global__ void __launch_bounds__(kSaThreads) sliding_attn_kernel(const uint16_t
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   pdl_wait();  // q, the caches and the mask come from earlier kernels
   const int rbase = c * kSaRows + warp * 8;
+  // every row is loaded together with the mask (one round trip, not two); rows the mask
+  // excludes are never used
   const float mv = lane < 8 ? mask[rbase + lane] : 0.f;
-  const uint32_t valid = __ballot_sync(0xffffffffu, mv > 0.f) & 0xFFu;
   const uint16_t* qh = q + static_cast<size_t>(h) * GS * DS + lane * 8;
   const uint4 q0 = *reinterpret_cast<const uint4*>(qh);
   const uint4 q1 = *reinterpret_cast<const uint4*>(qh + DS);
   uint4 kk[8], vv[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    kk[j] = make_uint4(0u, 0u, 0u, 0u);
-    vv[j] = kk[j];
-    if ((valid >> j) & 1u) {
-      const size_t off = (static_cast<size_t>(rbase + j) * nkv + h) * DS + lane * 8;
-      kk[j] = *reinterpret_cast<const uint4*>(k + off);
-      vv[j] = *reinterpret_cast<const uint4*>(v + off);
-    }
+    const size_t off = (static_cast<size_t>(rbase + j) * nkv + h) * DS + lane * 8;
+    kk[j] = *reinterpret_cast<const uint4*>(k + off);
+    vv[j] = *reinterpret_cast<const uint4*>(v + off);
   }
+  const uint32_t valid = __ballot_sync(0xffffffffu, mv > 0.f) & 0xFFu;
   pdl_launch_dependents();
   float qa[8], qb[8];
   bf16x8_to_f32(q0, qa);
@@ -339,21 +338,37 @@ __global__ void __launch_bounds__(kSaThreads) sliding_attn_kernel(const uint16_t
   __syncthreads();
   if (!last) return;
   __threadfence();
+  // merge: every chunk's (m, l) in one parallel load, the weights once per q head, then
+  // each output's chunk values with independent loads
+  __shared__ float wsm[GS][kMaxSaChunks];
+  __shared__ float lsum[GS];
   const float* ph = part + static_cast<size_t>(h) * nchunks * kSaPart;
+  for (int i = tid; i < GS * nchunks; i += kSaThreads) {
+    const int cc = i / GS, hh = i % GS;
+    wsm[hh][cc] = __ldcg(ph + cc * kSaPart + hh);
+  }
+  __syncthreads();
+  if (warp < GS) {
+    float M = -CUDART_INF_F;
+    for (int cc = lane; cc < nchunks; cc += 32) M = fmaxf(M, wsm[warp][cc]);
+    M = warp_max(M);
+    float Ls = 0.f;
+    for (int cc = lane; cc < nchunks; cc += 32) {
+      const float m = wsm[warp][cc];
+      const float w = (m == -CUDART_INF_F) ? 0.f : expf(m - M);
+      Ls += w * __ldcg(ph + cc * kSaPart + GS + warp);
+      wsm[warp][cc] = w;
+    }
+    Ls = warp_sum(Ls);
+    if (lane == 0) lsum[warp] = Ls;
+  }
+  __syncthreads();
   for (int o = tid; o < GS * DS; o += kSaThreads) {
     const int hh = o / DS;
-    float M = -CUDART_INF_F;
-    for (int cc = 0; cc < nchunks; ++cc) M = fmaxf(M, __ldcg(ph + cc * kSaPart + hh));
-    float Ls = 0.f, acc = 0.f;
-    if (M != -CUDART_INF_F) {
-      for (int cc = 0; cc < nchunks; ++cc) {
-        const float m = __ldcg(ph + cc * kSaPart + hh);
-        if (m == -CUDART_INF_F) continue;
-        const float w = expf(m - M);
-        Ls += __ldcg(ph + cc * kSaPart + GS + hh) * w;
-        acc += __ldcg(ph + cc * kSaPart + 2 * GS + o) * w;
-      }
-    }
+    float acc = 0.f;
+#pragma unroll 8
+    for (int cc = 0; cc < nchunks; ++cc) acc += wsm[hh][cc] * __ldcg(ph + cc * kSaPart + 2 * GS + o);
+    const float Ls = lsum[hh];
     out[static_cast<size_t>(h) * GS * DS + o] = f32_to_bf16(Ls > 0.f ? acc / Ls : 0.f);
   }
   if (tid == 0) scr->attn_count[h] = 0u;
@@ -405,8 +420,10 @@ __device__ __forceinline__ const uint16_t* fa_row(const FaSrc& s, bool is_v, int
 __device__ __forceinline__ void fa_split(const FaSrc& s, int grid, int& n, int& rpc, int& nact) {
   n = s.n_dev != nullptr ? *s.n_dev : s.n_host;
   n = max(0, min(n, s.max_rows));
+  // at least two 32-row tiles per CTA: a partial (33 KB) costs about as much to write and
+  // merge as 16 rows of K and V cost to read
   rpc = (n + grid - 1) / grid;
-  rpc = max(8, (rpc + 7) & ~7);
+  rpc = max(64, (rpc + 31) & ~31);
   nact = (n + rpc - 1) / rpc;
 }
 
@@ -540,50 +557,59 @@ __global__ void __launch_bounds__(kFaThreads) fa_partial_kernel(const uint16_t* 
   }
 }
 
-// Two CTAs per head, 256 dims each: merge weights of the active partials in CTA order.
-__global__ void __launch_bounds__(256) fa_merge_kernel(const float* part, FaSrc src, int grid, float* running_sum,
-                                                       uint16_t* out) {
+// Four CTAs per head, 128 dims each: the active partials' (m, l) in one parallel load,
+// their weights once, then each output's partial values with independent loads, added in
+// CTA order.
+constexpr int kFaMergeThreads = 128;
+__global__ void __launch_bounds__(kFaMergeThreads) fa_merge_kernel(const float* part, FaSrc src, int grid,
+                                                                   float* running_sum, uint16_t* out) {
   __shared__ float w[kFaMaxCtas];
-  __shared__ float red[8];
+  __shared__ float red[kFaMergeThreads / 32];
   __shared__ float Mall, Lall;
-  const int h = blockIdx.x >> 1, half = blockIdx.x & 1, tid = threadIdx.x;
+  const int h = blockIdx.x >> 2, quarter = blockIdx.x & 3, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   pdl_wait();  // every partial of the previous kernel is written
   int n, rpc, nact;
   fa_split(src, grid, n, rpc, nact);
   float m = -CUDART_INF_F;
-  for (int p = tid; p < nact; p += 256) m = fmaxf(m, __ldcg(part + static_cast<size_t>(p) * kFaPart + h));
+  for (int p = tid; p < nact; p += kFaMergeThreads) {
+    const float mp = __ldcg(part + static_cast<size_t>(p) * kFaPart + h);
+    w[p] = mp;
+    m = fmaxf(m, mp);
+  }
   m = warp_max(m);
-  if ((tid & 31) == 0) red[tid >> 5] = m;
+  if (lane == 0) red[warp] = m;
   __syncthreads();
   if (tid == 0) {
     float x = red[0];
-    for (int i = 1; i < 8; ++i) x = fmaxf(x, red[i]);
+    for (int i = 1; i < kFaMergeThreads / 32; ++i) x = fmaxf(x, red[i]);
     Mall = x;
   }
   __syncthreads();
   const float M = Mall;
   float l = 0.f;
-  for (int p = tid; p < nact; p += 256) {
-    const float mp = __ldcg(part + static_cast<size_t>(p) * kFaPart + h);
+  for (int p = tid; p < nact; p += kFaMergeThreads) {
+    const float mp = w[p];
     const float wp = (mp == -CUDART_INF_F || M == -CUDART_INF_F) ? 0.f : expf(mp - M);
     w[p] = wp;
     l += wp * __ldcg(part + static_cast<size_t>(p) * kFaPart + GF + h);
   }
   l = warp_sum(l);
   __syncthreads();
-  if ((tid & 31) == 0) red[tid >> 5] = l;
+  if (lane == 0) red[warp] = l;
   __syncthreads();
   if (tid == 0) {
     float x = 0.f;
-    for (int i = 0; i < 8; ++i) x += red[i];
+    for (int i = 0; i < kFaMergeThreads / 32; ++i) x += red[i];
     Lall = x;
   }
   __syncthreads();
-  const int d = half * 256 + tid;
+  const int d = quarter * kFaMergeThreads + tid;
+  const float* src_o = part + 2 * GF + h * DF + d;
   float o = 0.f;
-  for (int p = 0; p < nact; ++p) o += w[p] * __ldcg(part + static_cast<size_t>(p) * kFaPart + 2 * GF + h * DF + d);
+#pragma unroll 8
+  for (int p = 0; p < nact; ++p) o += w[p] * __ldcg(src_o + static_cast<size_t>(p) * kFaPart);
   out[h * DF + d] = f32_to_bf16(Lall > 0.f ? o / Lall : 0.f);
-  if (half == 0 && tid == 0) running_sum[h] = 1.0f;
+  if (quarter == 0 && tid == 0) running_sum[h] = 1.0f;
 }
 
 // ---------------------------------------------------------------------------- launchers
@@ -624,7 +650,7 @@ static g4_status launch_full_attention(g4_ctx* ctx, const uint16_t* q, const FaS
                                        uint16_t* out) {
   static_assert(static_cast<size_t>(kFaMaxCtas) * kFaPart <= kAttnFloats, "partials fit the attention scratch");
   int nq = GF / ctx->tp_world;
-  const int want = (src.max_rows + 7) / 8;
+  const int want = (src.max_rows + 63) / 64;
   int grid = 2 * ctx->sm_count;
   if (grid > kFaMaxCtas) grid = kFaMaxCtas;
   if (want < grid) grid = want < 1 ? 1 : want;
@@ -637,7 +663,7 @@ static g4_status launch_full_attention(g4_ctx* ctx, const uint16_t* q, const FaS
                      "full attention partials");
   if (st != G4_OK) return st;
   void* a2[] = {(void*)&part, (void*)&s, (void*)&grid, (void*)&rsum, (void*)&out};
-  return launch_kernel(ctx, (const void*)fa_merge_kernel, dim3(2 * nq), dim3(256), 0, a2, false,
+  return launch_kernel(ctx, (const void*)fa_merge_kernel, dim3(4 * nq), dim3(kFaMergeThreads), 0, a2, false,
                        "full attention merge");
 }
 

@@ -1,5 +1,4 @@
-// FP8 attention projections of one decode token on the tensor cores, weights straight
-// from HBM into MMA fragments (no conversion, no shared-memory staging):
+// FP8 attention projections of one decode token on the tensor cores:
 //   project_qkv        (src/ops.rs:44-124): input RMSNorm -> Q/K/V rows -> per-head
 //                      RMSNorm, RoPE, q_out and the K/V cache rows (the head epilogue of
 //                      the reference's sliding/full rmsnorm + rope, src/device/*/).
@@ -8,31 +7,41 @@
 // Each output row is bf16(dot(x, e4m3 codes) * row scale), as the reference's
 // scaled_projection (scripts/generate_references.py:312-321).
 //
+// Weight stream.  Items are 16-row tiles (attention_output of a full layer: 16 rows x
+// half of K), which the checkpoint stores contiguously: the producer warp moves each with
+// ONE bulk copy (cp.async.bulk, L2 evict-first; 16 row copies for the half-K tiles) into a
+// 3-stage shared-memory ring, starting before the kernel waits for the previous one
+// (weights are never written by a kernel).  Large copies keep the copy engine's per-copy
+// cost out of the way and about 190 KB per SM in flight.  Four consumer warps share an
+// item, one K quarter each; the CTA's two warp groups take alternate items.
+//
 // Activation pieces.  x (bf16 after the norm) is scaled by 2^e so that max|x| lands in
 // [128, 256) and written as three E4M3 pieces p1 = e4m3(xs), p2 = e4m3(xs - p1),
 // p3 = e4m3(xs - p1 - p2) (each residual exact in f32): together 12+ significant bits, so
 // every bf16 element within 2^-6 of the maximum is represented exactly and smaller ones
 // to within 2^-18 of the maximum.  The pieces are the MMA's B columns 0..2
-// (mma.sync m16n8k32 e4m3 x e4m3 -> f32; E4M3 x E4M3 products are exact), the E4M3
-// weight codes the A operand as loaded: one 16-byte load per lane covers 16 k of a row,
-// and the k order inside each 64-k block is permuted the same way for A and B so every
-// fragment register comes from one load.  The three columns are added and scaled by 2^-e.
+// (mma.sync m16n8k32 e4m3 x e4m3 -> f32; E4M3 x E4M3 products are exact) and the E4M3
+// weight codes the A operand: one 16-byte shared-memory load per lane covers 16 k of a
+// row, and the k order inside each 64-k block is permuted the same way for A and B so
+// every fragment register comes from one load.  The three columns are added and scaled
+// by 2^-e.
 //
-// Work split.  Items are (16-row tile, K part); CTAs (one per SM) take contiguous item
-// ranges, their 8 warps items in turn; a warp loads all of an item's weights before any
-// arithmetic (the first item before waiting for the previous kernel).  Each item writes
-// its 16 partial row sums; the warp completing a head's last item runs that head's
-// epilogue (project_qkv), the last CTA the norm/residual tail (attention_output).  The
-// order of every sum is fixed, so results are deterministic.
+// Each item leaves its 16 partial row sums in global memory; project_qkv then runs one
+// small kernel over the heads (norm, RoPE, stores), attention_output's last CTA the
+// norm/residual tail.  Every sum has a fixed order, so results are deterministic.
 #include "g4_internal.h"
 #include "g4_common.cuh"
 
 namespace g4 {
 namespace fp8 {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 256;            // consumer threads (8 warps)
 constexpr int kWarps = kThreads / 32;
+constexpr int kAllThreads = kThreads + 32;  // + the producer warp
 constexpr int kMaxMats = 3;
+constexpr int kMaxStages = 3;
+constexpr int kQuarters = 4;              // consumer warps per item (K quarters)
+constexpr uint32_t kBarConsumers = 1;     // named barrier of the consumer warps
 
 struct Mat {
   const uint8_t* w;        // [rows, K] e4m3 codes
@@ -47,8 +56,8 @@ struct Args {
   const float* rsum;       // full attention_output: x / rsum[k / dh] first
   int dh;
   Mat m[kMaxMats];
-  int nmat, R, P;          // matrices, total rows, K parts per tile
-  float* part;             // [P][R] partial row sums
+  int nmat, R, P;          // matrices, total rows, K parts per tile (items per tile)
+  float* part;             // [R][P * kQuarters] partial row sums (a row's parts contiguous)
   Scratch* scr;
   int qkv;                 // 1: project_qkv head epilogues, 0: attention_output tail
   int D, nq, nk, nv;
@@ -61,6 +70,9 @@ struct Args {
   uint16_t* q_out;
   const uint16_t* post_w;
   uint16_t* residual;
+  int kc_bytes;            // K bytes of one item per row
+  int stages;
+  uint64_t budget_ns;
 };
 
 __device__ __forceinline__ void mma_e4m3(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -109,11 +121,12 @@ __device__ __forceinline__ float row_scale(const Args& a, int r) {
   return 0.f;
 }
 
+__device__ __forceinline__ void consumer_sync() { named_bar_sync(kBarConsumers, kThreads); }
 __device__ __forceinline__ float block_sum(float v, float* red) {
   v = warp_sum(v);
-  __syncthreads();
+  consumer_sync();
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
+  consumer_sync();
   float s = 0.f;
 #pragma unroll
   for (int w = 0; w < kWarps; ++w) s += red[w];
@@ -121,9 +134,9 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 __device__ __forceinline__ float block_max(float v, float* red) {
   v = warp_max(v);
-  __syncthreads();
+  consumer_sync();
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
+  consumer_sync();
   float s = 0.f;
 #pragma unroll
   for (int w = 0; w < kWarps; ++w) s = fmaxf(s, red[w]);
@@ -196,187 +209,300 @@ __device__ int stage_pieces(const Args& a, uint8_t* pieces, int kp, float* red) 
         *reinterpret_cast<uint2*>(pieces + k * kp + gi * 8) = make_uint2(p[k][0], p[k][1]);
     }
   }
-  __syncthreads();
+  consumer_sync();
   return e;
 }
 
-// Norm + RoPE + store of one head (lane l owns elements l + 32j).
-__device__ void head_epilogue(const Args& a, int head, int lane) {
-  constexpr int kMaxJ = 16;
-  const int J = a.D / 32;
-  float raw[kMaxJ];
-  const int row0 = head * a.D;
-  float ss = 0.f;
-#pragma unroll
-  for (int j = 0; j < kMaxJ; ++j) {
-    if (j < J) {
-      const int row = row0 + lane + 32 * j;
-      float acc = 0.f;
-      for (int p = 0; p < a.P; ++p) acc += __ldcg(a.part + static_cast<size_t>(p) * a.R + row);
-      raw[j] = round_bf16(acc * row_scale(a, row));
-      ss = __fadd_rn(ss, __fmul_rn(raw[j], raw[j]));
-    }
-  }
-  const float r = rms_factor(warp_sum(ss), a.D);
+// project_qkv head epilogue, one CTA per head (thread i owns elements i and i + 256 of a
+// 512-wide head): the row's K parts added in order, bf16(sum * row scale), the head's
+// RMSNorm (q/k weighted, v unweighted; a full layer's V is the unweighted norm of the raw
+// K head), RoPE with the partner element from shared memory, then q_out or the cache row
+// at the device byte offset.  Launched right after the projection kernel (programmatic
+// dependent launch); everything it reads from that kernel comes after the wait.
+__global__ void __launch_bounds__(256) qkv_head_kernel(const __grid_constant__ Args a) {
+  __shared__ float nsm[DF];
+  __shared__ float red[kWarps];
+  const int head = blockIdx.x, tid = threadIdx.x;
+  const int E2 = a.D / 256;  // elements per thread (1 or 2)
   const bool is_q = head < a.nq;
   const bool is_k = !is_q && head < a.nq + a.nk;
-  const int roff = __ldg(a.rope_off) / 2;
-  const int koff = __ldg(a.kv_off) / 2;
-  if (roff < 0 || static_cast<long long>(roff) + a.D > a.table_elems || koff < 0 ||
-      static_cast<long long>(koff) + static_cast<long long>(a.nv > 0 ? a.nk : 1) * a.D > a.cache_elems) {
-    if (lane == 0) atomicOr(&a.scr->status, DEV_ERR_BAD_OFFSET);
+  const uint16_t* nw = is_q ? a.qn_w : a.kn_w;
+  const int row0 = head * a.D;
+  // independent of the projection kernel: row scales, norm weights
+  float rsc[2], nwf[2];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    rsc[e] = nwf[e] = 0.f;
+    if (e < E2) {
+      const int i = tid + 256 * e;
+      rsc[e] = row_scale(a, row0 + i);
+      if (is_q || is_k) nwf[e] = bf16_to_f32(nw[i]);
+    }
+  }
+  pdl_wait();
+  const int roff = a.rope_off[0] / 2;
+  const int koff = a.kv_off[0] / 2;
+  float4 pv[2];
+  float cs[2] = {0.f, 0.f}, sn[2] = {0.f, 0.f};
+  const bool ok = !(roff < 0 || static_cast<long long>(roff) + a.D > a.table_elems || koff < 0 ||
+                    static_cast<long long>(koff) + static_cast<long long>(a.nv > 0 ? a.nk : 1) * a.D > a.cache_elems);
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    if (e < E2) {
+      const int i = tid + 256 * e;
+      pv[e] = __ldcg(reinterpret_cast<const float4*>(a.part) + row0 + i);
+      if (ok && (is_q || is_k)) {
+        cs[e] = bf16_to_f32(a.cosT[roff + i]);
+        sn[e] = bf16_to_f32(a.sinT[roff + i]);
+      }
+    }
+  }
+  float raw[2], ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    raw[e] = 0.f;
+    if (e < E2) {
+      raw[e] = round_bf16((((pv[e].x + pv[e].y) + pv[e].z) + pv[e].w) * rsc[e]);
+      ss = __fadd_rn(ss, __fmul_rn(raw[e], raw[e]));
+    }
+  }
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) tot += red[w];
+  const float r = rms_factor(tot, a.D);
+  if (!ok) {
+    if (tid == 0) atomicOr(&a.scr->status, DEV_ERR_BAD_OFFSET);
+    return;
+  }
+  if (!is_q && !is_k) {  // sliding V head: unweighted norm, no RoPE
+    const int vh = head - a.nq - a.nk;
+#pragma unroll
+    for (int e = 0; e < 2; ++e)
+      if (e < E2) a.vc[koff + vh * a.D + tid + 256 * e] = f32_to_bf16(__fmul_rn(raw[e], r));
     return;
   }
   if (is_k && a.nv == 0) {  // full (MQA) layer: V is the unweighted norm of the raw K head
-    for (int j = 0; j < J; ++j) a.vc[koff + lane + 32 * j] = f32_to_bf16(__fmul_rn(raw[j], r));
+#pragma unroll
+    for (int e = 0; e < 2; ++e)
+      if (e < E2) a.vc[koff + tid + 256 * e] = f32_to_bf16(__fmul_rn(raw[e], r));
   }
-  if (!is_q && !is_k) {     // sliding V head: unweighted norm, no RoPE
-    const int vh = head - a.nq - a.nk;
-    for (int j = 0; j < J; ++j) a.vc[koff + vh * a.D + lane + 32 * j] = f32_to_bf16(__fmul_rn(raw[j], r));
-    return;
+  float n[2];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    n[e] = 0.f;
+    if (e < E2) {
+      n[e] = round_bf16(__fmul_rn(__fmul_rn(raw[e], r), nwf[e]));
+      nsm[tid + 256 * e] = n[e];
+    }
   }
-  const uint16_t* nw = is_q ? a.qn_w : a.kn_w;
-  float n[kMaxJ];
+  __syncthreads();
+  const int half = a.D / 2;
+  uint16_t* dst = is_q ? a.q_out + head * a.D : a.kc + koff + (head - a.nq) * a.D;
 #pragma unroll
-  for (int j = 0; j < kMaxJ; ++j)
-    if (j < J) n[j] = round_bf16(__fmul_rn(__fmul_rn(raw[j], r), bf16_to_f32(nw[lane + 32 * j])));
-  const int half = J / 2;
-#pragma unroll
-  for (int j = 0; j < kMaxJ; ++j) {
-    if (j < J) {
-      const int i = lane + 32 * j;
-      const int pj = (j < half) ? j + half : j - half;
-      float partner = 0.f;
-#pragma unroll
-      for (int q = 0; q < kMaxJ; ++q)
-        if (q == pj) partner = n[q];
-      const float c = bf16_to_f32(a.cosT[roff + i]);
-      const float s = bf16_to_f32(a.sinT[roff + i]);
-      const float o = round_bf16(__fadd_rn(round_bf16(__fmul_rn(n[j], c)), round_bf16(__fmul_rn(partner, s))));
-      if (is_q)
-        a.q_out[head * a.D + i] = f32_to_bf16(o);
-      else
-        a.kc[koff + (head - a.nq) * a.D + i] = f32_to_bf16(o);
+  for (int e = 0; e < 2; ++e) {
+    if (e < E2) {
+      const int i = tid + 256 * e;
+      const float partner = nsm[i < half ? i + half : i - half];
+      const float o = round_bf16(__fadd_rn(round_bf16(__fmul_rn(n[e], cs[e])), round_bf16(__fmul_rn(partner, sn[e]))));
+      dst[i] = f32_to_bf16(o);
     }
   }
 }
 
 // attention_output tail (one CTA): y = bf16(sum * row scale), RMSNorm, residual add.
-__device__ void oproj_tail(const Args& a, float* red) {
-  constexpr int kPer = (H + kThreads - 1) / kThreads;
-  float y[kPer];
+// Thread c < H/8 owns rows [8c, 8c + 8) of chunk c (two chunks per thread); every load is
+// issued before any store.
+template <int P>
+__device__ __noinline__ void oproj_tail(const Args& a, float* red) {
+  constexpr int kChunks = H / 8, kPer = (kChunks + kThreads - 1) / kThreads;
+  float y[kPer][8];
+  uint4 wv[kPer], rv[kPer], sv[kPer];
+  float4 pp[kPer][2 * P];
+#pragma unroll
+  for (int c = 0; c < kPer; ++c) {
+    const int ch = threadIdx.x + c * kThreads;
+    if (ch < kChunks) {
+      const float4* pr = reinterpret_cast<const float4*>(a.part + static_cast<size_t>(ch) * 8 * P);  // P parts per row
+#pragma unroll
+      for (int i = 0; i < 2 * P; ++i) pp[c][i] = __ldcg(pr + i);
+      sv[c] = __ldg(reinterpret_cast<const uint4*>(a.m[0].scale) + ch);
+      wv[c] = __ldg(reinterpret_cast<const uint4*>(a.post_w) + ch);
+      rv[c] = *reinterpret_cast<const uint4*>(a.residual + 8 * ch);
+    }
+  }
   float ss = 0.f;
 #pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    const int row = threadIdx.x + j * kThreads;
-    y[j] = 0.f;
-    if (row < H) {
-      float acc = 0.f;
-      for (int p = 0; p < a.P; ++p) acc += __ldcg(a.part + static_cast<size_t>(p) * a.R + row);
-      y[j] = round_bf16(acc * bf16_to_f32(a.m[0].scale[row]));
-      ss = __fadd_rn(ss, __fmul_rn(y[j], y[j]));
+  for (int c = 0; c < kPer; ++c) {
+    const int ch = threadIdx.x + c * kThreads;
+    if (ch < kChunks) {
+      const uint32_t sw[4] = {sv[c].x, sv[c].y, sv[c].z, sv[c].w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        // row i's P parts: float4s [i*P/4, (i+1)*P/4) of the chunk
+        float acc = 0.f;
+#pragma unroll
+        for (int q = 0; q < P / 4; ++q) {
+          const float4 f = pp[c][i * P / 4 + q];
+          acc += ((f.x + f.y) + f.z) + f.w;
+        }
+        const float sc = bf16_to_f32(static_cast<uint16_t>((i & 1) ? sw[i >> 1] >> 16 : sw[i >> 1] & 0xFFFFu));
+        y[c][i] = round_bf16(acc * sc);
+        ss = __fadd_rn(ss, __fmul_rn(y[c][i], y[c][i]));
+      }
     }
   }
   const float r = rms_factor(block_sum(ss, red), H);
 #pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    const int row = threadIdx.x + j * kThreads;
-    if (row < H) {
-      const float nb = round_bf16(__fmul_rn(__fmul_rn(y[j], r), bf16_to_f32(a.post_w[row])));
-      a.residual[row] = f32_to_bf16(__fadd_rn(bf16_to_f32(a.residual[row]), nb));
+  for (int c = 0; c < kPer; ++c) {
+    const int ch = threadIdx.x + c * kThreads;
+    if (ch < kChunks) {
+      const uint32_t rw[4] = {rv[c].x, rv[c].y, rv[c].z, rv[c].w}, ww[4] = {wv[c].x, wv[c].y, wv[c].z, wv[c].w};
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint16_t h2[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const float res = bf16_to_f32(static_cast<uint16_t>(j ? rw[i] >> 16 : rw[i] & 0xFFFFu));
+          const float pw = bf16_to_f32(static_cast<uint16_t>(j ? ww[i] >> 16 : ww[i] & 0xFFFFu));
+          const float nb = round_bf16(__fmul_rn(__fmul_rn(y[c][2 * i + j], r), pw));
+          h2[j] = f32_to_bf16(__fadd_rn(res, nb));
+        }
+        o[i] = pack_u16x2(h2[0], h2[1]);
+      }
+      *reinterpret_cast<uint4*>(a.residual + 8 * ch) = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
 }
 
+__device__ __forceinline__ uint4 lds128_at(uint32_t addr) { return lds128(addr); }
+
 template <int BPP>
-__global__ void __launch_bounds__(kThreads, 1) fp8_gemv_kernel(const Args a) {
-  extern __shared__ __align__(16) uint8_t fp8_pieces[];
+__global__ void __launch_bounds__(kAllThreads, 1) fp8_gemv_kernel(const __grid_constant__ Args a) {
+  extern __shared__ __align__(128) uint8_t fp8_smem[];
+  __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
   __shared__ float red[kWarps];
-  __shared__ int s_done, s_last;
+  __shared__ int s_last;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
-  const int kp = a.K + 16;  // piece row stride: the three rows start in different banks
+  const int kp = a.K + 16;                    // piece row stride: the three rows start in different banks
+  uint8_t* pieces = fp8_smem;
+  uint8_t* ring = fp8_smem + (3 * kp + 127) / 128 * 128;
+  const uint32_t stage_bytes = 16u * static_cast<uint32_t>(a.kc_bytes);
+  const int S = a.stages;
   const int N = (a.R / 16) * a.P;
   const int i0 = static_cast<int>(static_cast<long long>(blockIdx.x) * N / gridDim.x);
   const int i1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * N / gridDim.x);
-  if (tid == 0) s_done = 0;
-  uint4 wa[BPP], wb[BPP];
-  const uint64_t pol = l2_evict_first_policy();
-  auto load_item = [&](int it) {
-    const int tile = it / a.P, p = it % a.P;
-    int mi;
-    const uint8_t* ra = row_ptr(a, tile * 16 + g, mi) + p * BPP * 64 + 16 * t;
-    const uint8_t* rb = row_ptr(a, tile * 16 + g + 8, mi) + p * BPP * 64 + 16 * t;
-#pragma unroll
-    for (int b = 0; b < BPP; ++b) {
-      wa[b] = ld_stream(ra + 64 * b, pol);
-      wb[b] = ld_stream(rb + 64 * b, pol);
+  const int n_items = i1 - i0;
+  const uint64_t deadline = global_ns() + a.budget_ns;
+  if (tid == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kQuarters);
     }
-  };
-  int item = i0 + warp;
-  if (item < i1) load_item(item);  // weights are never written by an earlier kernel
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kWarps) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      const uint64_t pol = l2_evict_first_policy();
+      int issued = 0;
+      bool ok = true;
+      for (int j = 0; j < n_items; ++j) {
+        const int st = j % S;
+        if (j >= S && !mbar_wait(&empty[st], ((j / S) - 1) & 1, deadline)) {
+          atomicOr(&a.scr->status, DEV_ERR_TIMEOUT_MBAR);
+          ok = false;
+          break;
+        }
+        const int it = i0 + j, tile = it / a.P, p = it % a.P;
+        uint8_t* dst = ring + st * stage_bytes;
+        int mi;
+        const uint8_t* src = row_ptr(a, tile * 16, mi) + static_cast<size_t>(p) * a.kc_bytes;
+        mbar_arrive_expect_tx(&full[st], stage_bytes);
+        if (a.P == 1) {  // 16 whole rows: one contiguous range
+          bulk_g2s(dst, src, stage_bytes, &full[st], pol);
+        } else {
+          for (int r = 0; r < 16; ++r)
+            bulk_g2s(dst + r * a.kc_bytes, src + static_cast<size_t>(r) * a.K, static_cast<uint32_t>(a.kc_bytes),
+                     &full[st], pol);
+        }
+        issued = j + 1;
+      }
+      // every copy lands before the CTA may exit (the consumers wait for all in a normal run)
+      if (!ok) {
+        for (int j = (issued > S ? issued - S : 0); j < issued; ++j)
+          if (!mbar_wait(&full[j % S], (j / S) & 1, deadline + a.budget_ns)) break;
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ consumers
   pdl_wait();
-  const int e = stage_pieces(a, fp8_pieces, kp, red);
+  const int e = stage_pieces(a, pieces, kp, red);
   const float unscale = ldexpf(1.0f, -e);
-  while (item < i1) {
-    const int tile = item / a.P, p = item % a.P;
+  const int grp = warp / kQuarters, q = warp % kQuarters;
+  const int qbytes = a.kc_bytes / kQuarters;  // = BPP * 64
+  const int nparts = a.P * kQuarters;
+  const uint32_t ring_s = smem_u32(ring);
+  for (int j = grp; j < n_items; j += kWarps / kQuarters) {
+    const int st = j % S;
+    if (!mbar_wait(&full[st], (j / S) & 1, deadline)) {
+      atomicOr(&a.scr->status, DEV_ERR_TIMEOUT_MBAR);
+      break;
+    }
+    const int it = i0 + j, tile = it / a.P, p = it % a.P;
+    const uint32_t ra = ring_s + st * stage_bytes + g * a.kc_bytes + q * qbytes + 16 * t;
+    const uint32_t rb = ra + 8 * a.kc_bytes;
+    const uint8_t* pc = pieces + g * kp + p * a.kc_bytes + q * qbytes + 16 * t;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    const uint8_t* pc = fp8_pieces + g * kp + p * BPP * 64 + 16 * t;
 #pragma unroll
     for (int b = 0; b < BPP; ++b) {
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int m = 0; m < 2; ++m) {
-        uint2 bv = make_uint2(0u, 0u);
-        if (g < 3) bv = *reinterpret_cast<const uint2*>(pc + 64 * b + 8 * m);
-        if (m == 0)
-          mma_e4m3(d, wa[b].x, wb[b].x, wa[b].y, wb[b].y, bv.x, bv.y);
-        else
-          mma_e4m3(d, wa[b].z, wb[b].z, wa[b].w, wb[b].w, bv.x, bv.y);
+      const uint4 wa = lds128(ra + 64 * b), wb = lds128(rb + 64 * b);
+      uint2 bv0 = make_uint2(0u, 0u), bv1 = bv0;
+      if (g < 3) {
+        bv0 = *reinterpret_cast<const uint2*>(pc + 64 * b);
+        bv1 = *reinterpret_cast<const uint2*>(pc + 64 * b + 8);
       }
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      mma_e4m3(d, wa.x, wb.x, wa.y, wb.y, bv0.x, bv0.y);
+      mma_e4m3(d, wa.z, wb.z, wa.w, wb.w, bv1.x, bv1.y);
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[i] += d[i];
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
     // columns 0..2 are the pieces: the quad's lanes 0 (cols 0,1) and 1 (col 2)
     float lo = (t == 0) ? acc[0] + acc[1] : (t == 1 ? acc[0] : 0.f);
     float hi = (t == 0) ? acc[2] + acc[3] : (t == 1 ? acc[2] : 0.f);
     lo += __shfl_xor_sync(0xffffffffu, lo, 1);
     hi += __shfl_xor_sync(0xffffffffu, hi, 1);
     if (t == 0) {
-      float* dst = a.part + static_cast<size_t>(p) * a.R + tile * 16 + g;
+      float* dst = a.part + static_cast<size_t>(tile * 16 + g) * nparts + p * kQuarters + q;
       dst[0] = lo * unscale;
-      dst[8] = hi * unscale;
+      dst[8 * nparts] = hi * unscale;
     }
-    const int next = item + kWarps;
-    if (next < i1) load_item(next);
-    else pdl_launch_dependents();
-    if (a.qkv) {
-      __syncwarp();
-      const int head = tile * 16 / a.D;
-      uint32_t old = 0;
-      if (lane == 0) {
-        __threadfence();
-        old = atom_add_acq_rel_gpu(&a.scr->head_count[head], 1u);
-      }
-      old = __shfl_sync(0xffffffffu, old, 0);
-      if (old + 1 == static_cast<uint32_t>(a.D / 16 * a.P)) {
-        __threadfence();
-        head_epilogue(a, head, lane);
-        if (lane == 0) a.scr->head_count[head] = 0u;
-      }
-    }
-    item = next;
   }
+  pdl_launch_dependents();
   if (a.qkv) return;
   // attention_output: the last CTA to finish runs the tail
-  __syncthreads();
+  consumer_sync();
   if (tid == 0) {
     __threadfence();
     s_last = atom_add_acq_rel_gpu(&a.scr->proj_done, 1u) == gridDim.x - 1;
   }
-  __syncthreads();
+  consumer_sync();
   if (!s_last) return;
   __threadfence();
-  oproj_tail(a, red);
+  if (nparts == 8)
+    oproj_tail<8>(a, red);
+  else
+    oproj_tail<4>(a, red);
   if (tid == 0) a.scr->proj_done = 0u;
 }
 
@@ -385,12 +511,22 @@ __global__ void __launch_bounds__(kThreads, 1) fp8_gemv_kernel(const Args a) {
 static g4_status launch_fp8(g4_ctx* ctx, fp8::Args& a, int bpp) {
   a.scr = ctx->buf.scratch;
   a.part = ctx->buf.part;
-  if (static_cast<size_t>(a.P) * a.R > kPartFloats)
+  a.budget_ns = ctx->wait_budget_ns;
+  if (static_cast<size_t>(a.P) * fp8::kQuarters * a.R > kPartFloats)
     return fail(ctx, G4_ERR_UNSUPPORTED, "fp8 projection: partial sums exceed the scratch");
-  const size_t smem = 3 * static_cast<size_t>(a.K + 16);
+  a.kc_bytes = a.K / a.P;
+  const size_t pieces = (3 * static_cast<size_t>(a.K + 16) + 127) / 128 * 128;
+  const size_t stage = 16 * static_cast<size_t>(a.kc_bytes);
+  a.stages = fp8::kMaxStages;
+  const size_t smem = pieces + stage * a.stages;
   const void* fn = bpp == 15 ? (const void*)fp8::fp8_gemv_kernel<15> : (const void*)fp8::fp8_gemv_kernel<16>;
+  g4_status st = allow_max_dynamic_smem(ctx, fn, smem, "fp8 projection");
+  if (st != G4_OK) return st;
   void* args[] = {(void*)&a};
-  return launch_kernel(ctx, fn, dim3(ctx->sm_count), dim3(fp8::kThreads), smem, args, false, "fp8 projection");
+  st = launch_kernel(ctx, fn, dim3(ctx->sm_count), dim3(fp8::kAllThreads), smem, args, false, "fp8 projection");
+  if (st != G4_OK || !a.qkv) return st;
+  return launch_kernel(ctx, (const void*)fp8::qkv_head_kernel, dim3(a.nq + a.nk + a.nv), dim3(256), 0, args, false,
+                       "qkv heads");
 }
 
 // project_qkv with FP8 weights on one GPU (the caller routes other cases elsewhere).
@@ -411,7 +547,7 @@ g4_status launch_qkv_fp8(g4_ctx* ctx, bool full, const uint16_t* x, const uint8_
   const int rows[3] = {a.nq * a.D, a.nk * a.D, a.nv * a.D};
   for (int i = 0; i < a.nmat; ++i) a.m[i] = fp8::Mat{w[i], rs[i], rows[i]};
   a.R = rows[0] + rows[1] + rows[2];
-  a.P = 4;  // 4 parts of 960 k = 15 blocks
+  a.P = 1;  // whole 16-row tiles; 4 K quarters of 960 = 15 blocks (the head kernel reads a row's 4 parts as one float4)
   a.qkv = 1;
   a.qn_w = qn_w;
   a.kn_w = kn_w;
@@ -439,7 +575,7 @@ g4_status launch_oproj_fp8(g4_ctx* ctx, bool full, const uint16_t* x, const floa
   a.nmat = 1;
   a.m[0] = fp8::Mat{w, row_scale, H};
   a.R = H;
-  a.P = a.K / 1024;  // parts of 16 blocks
+  a.P = a.K / 4096;  // sliding: whole 16-row tiles; full: half rows (quarters of 1024 = 16 blocks)
   a.qkv = 0;
   a.post_w = post_w;
   a.residual = residual;

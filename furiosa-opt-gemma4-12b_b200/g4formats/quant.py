@@ -11,7 +11,10 @@ benchmark's N(0, sigma) weight configurations, with the usual NVFP4 recipe:
     code   = e2m1(W * g / s_b)                       (round-to-nearest-even, saturate 6)
     W     ~= code * s_b / g                          (kernels multiply by 1/g)
 
-Everything runs in torch on the tensor's device (CPU or GPU).
+Everything runs in torch on the tensor's device (CPU or GPU) with the same bits on both:
+every operation is an exactly rounded elementwise op or an exact reduction, and a
+division by a constant is written as a tensor division (torch's CUDA kernels turn a
+division by a Python number into a multiplication by its reciprocal, the CPU's do not).
 """
 
 from __future__ import annotations
@@ -43,15 +46,20 @@ def pack_e2m1(codes: torch.Tensor) -> torch.Tensor:
     return (c[..., 0::2] | (c[..., 1::2] << 4)).contiguous()
 
 
+def _div(x: torch.Tensor, c: float) -> torch.Tensor:
+    """x / c, correctly rounded on the CPU and on a GPU alike."""
+    return x / torch.full_like(x, c)
+
+
 def quantize_nvfp4(w: torch.Tensor):
     """[N, K] float weights -> (packed u8 [N, K/2], block scales u8 [N, K/16], 1/g f32 [1])."""
     w = w.float()
     n, k = w.shape
     amax = w.abs().max().clamp_min(1e-30)
-    g = (448.0 * 6.0) / amax
+    g = torch.reciprocal(amax) * (448.0 * 6.0)  # what `2688.0 / amax` computes on either device
     blocks = w.view(n, k // 16, 16)
     bmax = blocks.abs().amax(dim=-1)
-    s = (bmax / 6.0 * g).clamp(max=448.0).to(torch.float8_e4m3fn)
+    s = (_div(bmax, 6.0) * g).clamp(max=448.0).to(torch.float8_e4m3fn)
     sf = s.float()
     scaled = torch.where(sf[..., None] > 0, blocks * g / sf[..., None].clamp_min(1e-30), torch.zeros_like(blocks))
     codes = e2m1_encode(scaled).view(n, k)
@@ -64,7 +72,7 @@ def quantize_fp8_rows(w: torch.Tensor):
     (src/host/load.rs:22-56): W ~= code * scale_row."""
     w = w.float()
     rmax = w.abs().amax(dim=1).clamp_min(1e-30)
-    scale = (rmax / 448.0).to(torch.bfloat16)
+    scale = _div(rmax, 448.0).to(torch.bfloat16)
     codes = (w / scale.float()[:, None]).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
     return codes.view(torch.uint8).contiguous(), scale.contiguous()
 
