@@ -300,6 +300,12 @@ g4_status g4_ctx_destroy(g4_ctx* ctx) {
   cudaFree(ctx->buf.tc_seg);
   cudaFree(ctx->buf.tc_ptag);
   cudaFree(ctx->buf.tc_htag);
+  cudaFree(ctx->prefill.xq);
+  cudaFree(ctx->prefill.h);
+  cudaFree(ctx->prefill.hq);
+  cudaFree(ctx->prefill.y);
+  cudaFree(ctx->prefill.ginv);
+  cudaFree(ctx->prefill.down_sf);
   delete ctx;
   return G4_OK;
 }
@@ -358,6 +364,13 @@ g4_status g4_ctx_set_mlp_kernel(g4_ctx* ctx, int kind) {
   if (kind != G4_MLP_AUTO && kind != G4_MLP_STREAM && kind != G4_MLP_TENSOR)
     return fail(ctx, G4_ERR_BAD_ARG, "mlp kernel must be G4_MLP_AUTO, G4_MLP_STREAM or G4_MLP_TENSOR");
   ctx->mlp_kernel = kind;
+  return G4_OK;
+}
+
+g4_status g4_ctx_set_prefill_pieces(g4_ctx* ctx, int pieces) {
+  G4_CHECK_CTX(ctx);
+  if (pieces < 1 || pieces > 3) return fail(ctx, G4_ERR_BAD_ARG, "prefill pieces must be 1, 2 or 3");
+  ctx->prefill_pieces = pieces;
   return G4_OK;
 }
 
@@ -567,6 +580,25 @@ g4_status g4_decoder_feedforward(g4_ctx* ctx, g4_bf16* residual, const g4_bf16* 
                                     down_weight_packed, up_weight_scale, gate_weight_scale, down_weight_scale,
                                     up_global_scale, gate_global_scale, down_global_scale, post_ff_rms_weight,
                                     layer_scalar);
+}
+
+g4_status g4_decoder_feedforward_prefill(g4_ctx* ctx, int n_tokens, g4_bf16* residual,
+                                         const g4_bf16* pre_ff_rms_weight, const g4_f4x2* up_weight_packed,
+                                         const g4_f4x2* gate_weight_packed, const g4_f4x2* down_weight_packed,
+                                         const g4_f8e4m3* up_weight_scale, const g4_f8e4m3* gate_weight_scale,
+                                         const g4_f8e4m3* down_weight_scale, const float* up_global_scale,
+                                         const float* gate_global_scale, const float* down_global_scale,
+                                         const g4_bf16* post_ff_rms_weight, const g4_bf16* layer_scalar) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, residual, pre_ff_rms_weight, up_weight_packed, gate_weight_packed, down_weight_packed,
+                  up_weight_scale, gate_weight_scale, down_weight_scale, post_ff_rms_weight, layer_scalar);
+  G4_REQUIRE_SCALARS(ctx, up_global_scale, gate_global_scale, down_global_scale);
+  if (n_tokens <= 0 || n_tokens > G4_PREFILL_MAX_TOKENS)
+    return fail(ctx, G4_ERR_BAD_ARG, "n_tokens must be in [1, G4_PREFILL_MAX_TOKENS]");
+  return launch_prefill_feedforward(ctx, n_tokens, residual, pre_ff_rms_weight, up_weight_packed,
+                                    gate_weight_packed, down_weight_packed, up_weight_scale, gate_weight_scale,
+                                    down_weight_scale, up_global_scale, gate_global_scale, down_global_scale,
+                                    post_ff_rms_weight, layer_scalar);
 }
 
 g4_status g4_final_norm_and_logits(g4_ctx* ctx, const g4_bf16* input, const g4_bf16* rms_weight,

@@ -39,7 +39,7 @@ constexpr int kThreads = 256;            // consumer threads (8 warps)
 constexpr int kWarps = kThreads / 32;
 constexpr int kAllThreads = kThreads + 32;  // + the producer warp
 constexpr int kMaxMats = 3;
-constexpr int kMaxStages = 3;
+constexpr int kMaxStages = 8;
 constexpr int kQuarters = 4;              // consumer warps per item (K quarters)
 constexpr uint32_t kBarConsumers = 1;     // named barrier of the consumer warps
 
@@ -312,70 +312,59 @@ __global__ void __launch_bounds__(256) qkv_head_kernel(const __grid_constant__ A
   }
 }
 
-// attention_output tail (one CTA): y = bf16(sum * row scale), RMSNorm, residual add.
-// Thread c < H/8 owns rows [8c, 8c + 8) of chunk c (two chunks per thread); every load is
-// issued before any store.
+// attention_output tail: one CTA, thread c owns rows [8c, 8c + 8): the row's K parts
+// added in order, y = bf16(sum * row scale), RMSNorm over the 3840 rows, residual add in
+// place.  Launched right after the projection kernel; the weights it reads (row scales,
+// norm weight) are loaded before the wait, the partial sums and the residual after.
+constexpr int kTailThreads = H / 8;  // 480
 template <int P>
-__device__ __noinline__ void oproj_tail(const Args& a, float* red) {
-  constexpr int kChunks = H / 8, kPer = (kChunks + kThreads - 1) / kThreads;
-  float y[kPer][8];
-  uint4 wv[kPer], rv[kPer], sv[kPer];
-  float4 pp[kPer][2 * P];
+__global__ void __launch_bounds__(kTailThreads) oproj_tail_kernel(const __grid_constant__ Args a) {
+  __shared__ float red[kTailThreads / 32];
+  const int ch = threadIdx.x;
+  const uint4 sv = __ldg(reinterpret_cast<const uint4*>(a.m[0].scale) + ch);
+  const uint4 wv = __ldg(reinterpret_cast<const uint4*>(a.post_w) + ch);
+  pdl_wait();
+  float4 pp[2 * P];
+  const float4* pr = reinterpret_cast<const float4*>(a.part + static_cast<size_t>(ch) * 8 * P);
 #pragma unroll
-  for (int c = 0; c < kPer; ++c) {
-    const int ch = threadIdx.x + c * kThreads;
-    if (ch < kChunks) {
-      const float4* pr = reinterpret_cast<const float4*>(a.part + static_cast<size_t>(ch) * 8 * P);  // P parts per row
+  for (int i = 0; i < 2 * P; ++i) pp[i] = __ldcg(pr + i);
+  const uint4 rv = *reinterpret_cast<const uint4*>(a.residual + 8 * ch);
+  const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+  float y[8], ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < 2 * P; ++i) pp[c][i] = __ldcg(pr + i);
-      sv[c] = __ldg(reinterpret_cast<const uint4*>(a.m[0].scale) + ch);
-      wv[c] = __ldg(reinterpret_cast<const uint4*>(a.post_w) + ch);
-      rv[c] = *reinterpret_cast<const uint4*>(a.residual + 8 * ch);
+  for (int i = 0; i < 8; ++i) {
+    float acc = 0.f;
+#pragma unroll
+    for (int q = 0; q < P / 4; ++q) {
+      const float4 f = pp[i * P / 4 + q];
+      acc += ((f.x + f.y) + f.z) + f.w;
     }
+    const float sc = bf16_to_f32(static_cast<uint16_t>((i & 1) ? sw[i >> 1] >> 16 : sw[i >> 1] & 0xFFFFu));
+    y[i] = round_bf16(acc * sc);
+    ss = __fadd_rn(ss, __fmul_rn(y[i], y[i]));
   }
-  float ss = 0.f;
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
 #pragma unroll
-  for (int c = 0; c < kPer; ++c) {
-    const int ch = threadIdx.x + c * kThreads;
-    if (ch < kChunks) {
-      const uint32_t sw[4] = {sv[c].x, sv[c].y, sv[c].z, sv[c].w};
+  for (int w = 0; w < kTailThreads / 32; ++w) tot += red[w];
+  const float r = rms_factor(tot, H);
+  const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
+  uint32_t o[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        // row i's P parts: float4s [i*P/4, (i+1)*P/4) of the chunk
-        float acc = 0.f;
+  for (int i = 0; i < 4; ++i) {
+    uint16_t h2[2];
 #pragma unroll
-        for (int q = 0; q < P / 4; ++q) {
-          const float4 f = pp[c][i * P / 4 + q];
-          acc += ((f.x + f.y) + f.z) + f.w;
-        }
-        const float sc = bf16_to_f32(static_cast<uint16_t>((i & 1) ? sw[i >> 1] >> 16 : sw[i >> 1] & 0xFFFFu));
-        y[c][i] = round_bf16(acc * sc);
-        ss = __fadd_rn(ss, __fmul_rn(y[c][i], y[c][i]));
-      }
+    for (int j = 0; j < 2; ++j) {
+      const float res = bf16_to_f32(static_cast<uint16_t>(j ? rw[i] >> 16 : rw[i] & 0xFFFFu));
+      const float pw = bf16_to_f32(static_cast<uint16_t>(j ? ww[i] >> 16 : ww[i] & 0xFFFFu));
+      const float nb = round_bf16(__fmul_rn(__fmul_rn(y[2 * i + j], r), pw));
+      h2[j] = f32_to_bf16(__fadd_rn(res, nb));
     }
+    o[i] = pack_u16x2(h2[0], h2[1]);
   }
-  const float r = rms_factor(block_sum(ss, red), H);
-#pragma unroll
-  for (int c = 0; c < kPer; ++c) {
-    const int ch = threadIdx.x + c * kThreads;
-    if (ch < kChunks) {
-      const uint32_t rw[4] = {rv[c].x, rv[c].y, rv[c].z, rv[c].w}, ww[4] = {wv[c].x, wv[c].y, wv[c].z, wv[c].w};
-      uint32_t o[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        uint16_t h2[2];
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const float res = bf16_to_f32(static_cast<uint16_t>(j ? rw[i] >> 16 : rw[i] & 0xFFFFu));
-          const float pw = bf16_to_f32(static_cast<uint16_t>(j ? ww[i] >> 16 : ww[i] & 0xFFFFu));
-          const float nb = round_bf16(__fmul_rn(__fmul_rn(y[c][2 * i + j], r), pw));
-          h2[j] = f32_to_bf16(__fadd_rn(res, nb));
-        }
-        o[i] = pack_u16x2(h2[0], h2[1]);
-      }
-      *reinterpret_cast<uint4*>(a.residual + 8 * ch) = make_uint4(o[0], o[1], o[2], o[3]);
-    }
-  }
+  *reinterpret_cast<uint4*>(a.residual + 8 * ch) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 __device__ __forceinline__ uint4 lds128_at(uint32_t addr) { return lds128(addr); }
@@ -385,7 +374,6 @@ __global__ void __launch_bounds__(kAllThreads, 1) fp8_gemv_kernel(const __grid_c
   extern __shared__ __align__(128) uint8_t fp8_smem[];
   __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
   __shared__ float red[kWarps];
-  __shared__ int s_last;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int kp = a.K + 16;                    // piece row stride: the three rows start in different banks
   uint8_t* pieces = fp8_smem;
@@ -489,44 +477,43 @@ __global__ void __launch_bounds__(kAllThreads, 1) fp8_gemv_kernel(const __grid_c
     }
   }
   pdl_launch_dependents();
-  if (a.qkv) return;
-  // attention_output: the last CTA to finish runs the tail
-  consumer_sync();
-  if (tid == 0) {
-    __threadfence();
-    s_last = atom_add_acq_rel_gpu(&a.scr->proj_done, 1u) == gridDim.x - 1;
-  }
-  consumer_sync();
-  if (!s_last) return;
-  __threadfence();
-  if (nparts == 8)
-    oproj_tail<8>(a, red);
-  else
-    oproj_tail<4>(a, red);
-  if (tid == 0) a.scr->proj_done = 0u;
 }
 
 }  // namespace fp8
 
-static g4_status launch_fp8(g4_ctx* ctx, fp8::Args& a, int bpp) {
+static g4_status launch_fp8(g4_ctx* ctx, fp8::Args& a) {
   a.scr = ctx->buf.scratch;
   a.part = ctx->buf.part;
   a.budget_ns = ctx->wait_budget_ns;
   if (static_cast<size_t>(a.P) * fp8::kQuarters * a.R > kPartFloats)
     return fail(ctx, G4_ERR_UNSUPPORTED, "fp8 projection: partial sums exceed the scratch");
   a.kc_bytes = a.K / a.P;
+  const int bpp = a.kc_bytes / fp8::kQuarters / 64;  // 64-k blocks per consumer warp and item
   const size_t pieces = (3 * static_cast<size_t>(a.K + 16) + 127) / 128 * 128;
   const size_t stage = 16 * static_cast<size_t>(a.kc_bytes);
-  a.stages = fp8::kMaxStages;
+  const size_t ring_budget = 200 * 1024 - pieces;
+  a.stages = static_cast<int>(ring_budget / stage);
+  if (a.stages > fp8::kMaxStages) a.stages = fp8::kMaxStages;
+  if (a.stages < 2) return fail(ctx, G4_ERR_UNSUPPORTED, "fp8 projection: shared-memory ring too small");
   const size_t smem = pieces + stage * a.stages;
-  const void* fn = bpp == 15 ? (const void*)fp8::fp8_gemv_kernel<15> : (const void*)fp8::fp8_gemv_kernel<16>;
+  const void* fn = bpp == 15 ? (const void*)fp8::fp8_gemv_kernel<15>
+                 : bpp == 8  ? (const void*)fp8::fp8_gemv_kernel<8>
+                             : nullptr;
+  if (fn == nullptr || bpp * 64 * fp8::kQuarters != a.kc_bytes)
+    return fail(ctx, G4_ERR_UNSUPPORTED, "fp8 projection: unsupported K split");
   g4_status st = allow_max_dynamic_smem(ctx, fn, smem, "fp8 projection");
   if (st != G4_OK) return st;
   void* args[] = {(void*)&a};
   st = launch_kernel(ctx, fn, dim3(ctx->sm_count), dim3(fp8::kAllThreads), smem, args, false, "fp8 projection");
-  if (st != G4_OK || !a.qkv) return st;
-  return launch_kernel(ctx, (const void*)fp8::qkv_head_kernel, dim3(a.nq + a.nk + a.nv), dim3(256), 0, args, false,
-                       "qkv heads");
+  if (st != G4_OK) return st;
+  if (a.qkv)
+    return launch_kernel(ctx, (const void*)fp8::qkv_head_kernel, dim3(a.nq + a.nk + a.nv), dim3(256), 0, args, false,
+                         "qkv heads");
+  const int nparts = a.P * fp8::kQuarters;
+  const void* tail = nparts == 16 ? (const void*)fp8::oproj_tail_kernel<16>
+                   : nparts == 8  ? (const void*)fp8::oproj_tail_kernel<8>
+                                  : (const void*)fp8::oproj_tail_kernel<4>;
+  return launch_kernel(ctx, tail, dim3(1), dim3(fp8::kTailThreads), 0, args, false, "o-proj tail");
 }
 
 // project_qkv with FP8 weights on one GPU (the caller routes other cases elsewhere).
@@ -561,7 +548,7 @@ g4_status launch_qkv_fp8(g4_ctx* ctx, bool full, const uint16_t* x, const uint8_
   a.cache_elems = cache_elems > 0 ? cache_elems
                                   : (full ? static_cast<long long>(TF) * DF : static_cast<long long>(TS) * NS * DS);
   a.q_out = q_out;
-  return launch_fp8(ctx, a, 15);
+  return launch_fp8(ctx, a);
 }
 
 // attention_output with FP8 weights on one GPU.
@@ -575,11 +562,11 @@ g4_status launch_oproj_fp8(g4_ctx* ctx, bool full, const uint16_t* x, const floa
   a.nmat = 1;
   a.m[0] = fp8::Mat{w, row_scale, H};
   a.R = H;
-  a.P = a.K / 4096;  // sliding: whole 16-row tiles; full: half rows (quarters of 1024 = 16 blocks)
+  a.P = a.K / 2048;  // items of 16 half rows (sliding) or quarter rows (full): quarters of 512 = 8 blocks
   a.qkv = 0;
   a.post_w = post_w;
   a.residual = residual;
-  return launch_fp8(ctx, a, 16);
+  return launch_fp8(ctx, a);
 }
 
 }  // namespace g4

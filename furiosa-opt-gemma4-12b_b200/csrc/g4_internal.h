@@ -71,6 +71,20 @@ struct DeviceBuffers {
   uint32_t* tc_htag = nullptr;  // [kHFloats]
 };
 
+// Batched prefill feed-forward scratch, grown to the largest token count seen and kept
+// until the context is destroyed: NVFP4 activations (codes then block scales), h in bf16,
+// the down projection's output, and the per-token 1/g of both quantised activations.
+struct PrefillBuffers {
+  int cap = 0;
+  uint8_t* xq = nullptr;     // [cap][H/2] codes, then [cap][H/16] scales
+  uint16_t* h = nullptr;     // [cap][lrows] (lrows: this rank's intermediate rows)
+  uint8_t* hq = nullptr;     // [cap][lrows/2] codes, then [cap][ld] scales (ld: lrows/16 rounded up to 16)
+  float* y = nullptr;        // [cap][H] the down projection's f32 sums
+  float* ginv = nullptr;     // [2][cap]
+  uint8_t* down_sf = nullptr;  // [H][ld] the down weights' scales re-laid out (when their rows
+                               // are not a multiple of 16 bytes: 8-way tensor parallel)
+};
+
 }  // namespace g4
 
 struct g4_ctx {
@@ -87,6 +101,8 @@ struct g4_ctx {
   bool pdl_ok = true;  // programmatic dependent launch accepted by the runtime
   int mlp_kernel = 0;  // G4_MLP_AUTO / G4_MLP_STREAM / G4_MLP_TENSOR
   g4::PeerXch peers = {};  // TP exchange buffers mapped from every rank (world 0: NCCL path)
+  g4::PrefillBuffers prefill;
+  int prefill_pieces = 2;  // NVFP4 pieces per prefill activation (1..3)
 };
 
 namespace g4 {
@@ -112,6 +128,12 @@ g4_status launch_decoder_feedforward_tc(g4_ctx* ctx, uint16_t* residual, const u
                                         const uint8_t* up_s, const uint8_t* gate_s, const uint8_t* down_s,
                                         const float* up_gs, const float* gate_gs, const float* down_gs,
                                         const uint16_t* post_w, const uint16_t* layer_scalar);
+// n tokens' MLP block at once on the tensor cores (g4_prefill.cu).
+g4_status launch_prefill_feedforward(g4_ctx* ctx, int n, uint16_t* residual, const uint16_t* pre_w,
+                                     const uint8_t* up_p, const uint8_t* gate_p, const uint8_t* down_p,
+                                     const uint8_t* up_s, const uint8_t* gate_s, const uint8_t* down_s,
+                                     const float* up_gs, const float* gate_gs, const float* down_gs,
+                                     const uint16_t* post_w, const uint16_t* layer_scalar);
 
 // Raises `fn`'s dynamic shared-memory limit to the device's opt-in maximum, once per
 // (kernel, device): every launch, whatever its layout (`need` bytes, checked), then fits,

@@ -70,6 +70,7 @@ LIB.g4_ctx_destroy.argtypes = [_vp]
 LIB.g4_ctx_set_stream.argtypes = [_vp, _vp]
 LIB.g4_ctx_set_wait_budget.argtypes = [_vp, _u32]
 LIB.g4_ctx_set_mlp_kernel.argtypes = [_vp, _i32]
+LIB.g4_ctx_set_prefill_pieces.argtypes = [_vp, _i32]
 LIB.g4_ctx_poll_device_status.argtypes = [_vp, ctypes.POINTER(_u32)]
 LIB.g4_nccl_unique_id.argtypes = [ctypes.c_char_p]
 LIB.g4_ctx_init_tp.argtypes = [_vp, _i32, _i32, ctypes.c_char_p]
@@ -178,11 +179,18 @@ class Context:
         return bool(out.value)
 
     MLP_KERNELS = {"auto": 0, "stream": 1, "tensor": 2}
+    prefill_pieces = 2  # the library's default (g4_ctx_set_prefill_pieces)
 
     def set_mlp_kernel(self, kind: str) -> None:
         """decoder_feedforward kernel of this context: "auto", "stream" (CUDA-core decode +
         mma.sync) or "tensor" (tcgen05 block-scaled FP4; one GPU only)."""
         self._check("g4_ctx_set_mlp_kernel", LIB.g4_ctx_set_mlp_kernel(self.handle, self.MLP_KERNELS[kind]))
+
+    def set_prefill_pieces(self, pieces: int) -> None:
+        """NVFP4 pieces per activation in decoder_feedforward_prefill: 1 (fastest, ~10 %
+        activation error), 2 (default, ~1 %) or 3 (~0.1 %)."""
+        self._check("g4_ctx_set_prefill_pieces", LIB.g4_ctx_set_prefill_pieces(self.handle, pieces))
+        self.prefill_pieces = pieces
 
     def set_wait_budget(self, timeout_us: int) -> None:
         self._check("g4_ctx_set_wait_budget", LIB.g4_ctx_set_wait_budget(self.handle, timeout_us))
@@ -233,6 +241,7 @@ LIB.g4_attention_gqa.argtypes = [_vp, _vp, _vp, _vp, _vp, _i32, _vp]
 LIB.g4_dequant_nvfp4.argtypes = [_vp, _vp, _vp, _i32, _i32, _vp]
 LIB.g4_dequant_fp8.argtypes = [_vp, _vp, _i64, _vp]
 LIB.g4_decoder_feedforward_noalloc.argtypes = [_vp, _u32] + [_vp] * 13
+LIB.g4_decoder_feedforward_prefill.argtypes = [_vp, _i32] + [_vp] * 13
 LIB.g4_decoder_feedforward_noalloc.restype = _i32
 
 
@@ -510,6 +519,42 @@ def decoder_feedforward(ctx: Context, residual, pre_ff_rms_weight, up_weight_pac
     ctx.call("g4_decoder_feedforward", residual, pre_ff_rms_weight, up_weight_packed, gate_weight_packed,
              down_weight_packed, up_weight_scale, gate_weight_scale, down_weight_scale, up_global_scale,
              gate_global_scale, down_global_scale, post_ff_rms_weight, layer_scalar)
+
+
+PREFILL_MAX_TOKENS = 65536
+
+
+def decoder_feedforward_prefill(ctx: Context, residual, pre_ff_rms_weight, up_weight_packed, gate_weight_packed,
+                                down_weight_packed, up_weight_scale, gate_weight_scale, down_weight_scale,
+                                up_global_scale, gate_global_scale, down_global_scale, post_ff_rms_weight,
+                                layer_scalar):
+    """decoder_feedforward for n tokens at once (g4_decoder_feedforward_prefill), in place
+    on residual [n, H]; the weights as for `decoder_feedforward`.  The activations are
+    quantised per token to NVFP4 for the block-scaled FP4 tensor cores."""
+    t = _t()
+    w = ctx.world
+    bf, u8, f8, f32 = (t.bfloat16,), (t.uint8,), (t.uint8, t.float8_e4m3fn), (t.float32,)
+    if residual.dim() != 2 or residual.shape[1] != H:
+        raise ValueError(f"residual: expected [n, {H}], got {list(residual.shape)}")
+    n = residual.shape[0]
+    if not 1 <= n <= PREFILL_MAX_TOKENS:
+        raise ValueError(f"residual: {n} tokens, expected 1..{PREFILL_MAX_TOKENS}")
+    _expect("residual", residual, n * H, bf)
+    _expect("pre_ff_rms_weight", pre_ff_rms_weight, H, bf)
+    _expect("up_weight_packed", up_weight_packed, L // w * H // 2, u8)
+    _expect("gate_weight_packed", gate_weight_packed, L // w * H // 2, u8)
+    _expect("down_weight_packed", down_weight_packed, H * L // w // 2, u8)
+    _expect("up_weight_scale", up_weight_scale, L // w * H // 16, f8)
+    _expect("gate_weight_scale", gate_weight_scale, L // w * H // 16, f8)
+    _expect("down_weight_scale", down_weight_scale, H * L // w // 16, f8)
+    _expect("up_global_scale", up_global_scale, 1, f32)
+    _expect("gate_global_scale", gate_global_scale, 1, f32)
+    _expect("down_global_scale", down_global_scale, 1, f32)
+    _expect("post_ff_rms_weight", post_ff_rms_weight, H, bf)
+    _expect("layer_scalar", layer_scalar, 8, bf)
+    ctx.call("g4_decoder_feedforward_prefill", ctypes.c_int32(n), residual, pre_ff_rms_weight, up_weight_packed,
+             gate_weight_packed, down_weight_packed, up_weight_scale, gate_weight_scale, down_weight_scale,
+             up_global_scale, gate_global_scale, down_global_scale, post_ff_rms_weight, layer_scalar)
 
 
 def final_norm_and_logits(ctx: Context, input, rms_weight, lm_head_weight, out):

@@ -117,6 +117,12 @@ g4_status g4_ctx_set_wait_budget(g4_ctx* ctx, uint32_t timeout_us);
  * for anywhere.  Same results within f32 rounding of the dot products. */
 enum { G4_MLP_AUTO = 0, G4_MLP_STREAM = 1, G4_MLP_TENSOR = 2 };
 g4_status g4_ctx_set_mlp_kernel(g4_ctx* ctx, int kind);
+
+/* How many NVFP4 pieces represent each activation in g4_decoder_feedforward_prefill
+ * (no reference counterpart): 1 (plain NVFP4 activations, fastest; ~10 % relative error
+ * per activation), 2 (the default; ~1 %, within the reference's bf16 tolerance on the
+ * MLP output) or 3 (~0.1 %).  The tensor-core work grows with the count. */
+g4_status g4_ctx_set_prefill_pieces(g4_ctx* ctx, int pieces);
 /* Synchronise the context's stream, then read and clear the device status word
  * (0 = no kernel reported a timeout or an out-of-range device offset).  Returns
  * G4_ERR_TIMEOUT / G4_ERR_BAD_ARG when a bit was set. */
@@ -224,6 +230,30 @@ g4_status g4_final_norm_and_logits(g4_ctx* ctx, const g4_bf16* input, const g4_b
 /* ------------------------------------------------------------------------------ */
 /* B200 additions (no single reference entry point; each names what it replaces)    */
 /* ------------------------------------------------------------------------------ */
+
+/* Batched prefill of ops::decoder_feedforward (src/ops.rs:213-253) for n_tokens
+ * positions at once, replacing the reference's one-position-per-dispatch prefill
+ * (src/host/generate.rs:194-211) for the MLP block.  residual is [n_tokens][H] bf16,
+ * updated in place; the weights are those of g4_decoder_feedforward (TP: the same
+ * shards).  The block runs as two block-scaled FP4 GEMMs on the tensor cores: the
+ * normed activations and h are quantised per token to NVFP4 with the weights' recipe
+ * (g = 6*448/max|row|, E4M3 scale per 16, E2M1 codes), so each token's result is the
+ * reference MLP applied to NVFP4-quantised activations.  Scratch for n_tokens is
+ * allocated by the context on first use and kept until g4_ctx_destroy; the call
+ * synchronises the device when it grows.  TP: each rank computes its intermediate
+ * rows and the ranks' down-projection sums are all-reduced in f32 over NCCL. */
+#define G4_PREFILL_MAX_TOKENS 65536
+g4_status g4_decoder_feedforward_prefill(g4_ctx* ctx, int n_tokens, g4_bf16* residual,
+                                         const g4_bf16* pre_ff_rms_weight,
+                                         const g4_f4x2* up_weight_packed,
+                                         const g4_f4x2* gate_weight_packed,
+                                         const g4_f4x2* down_weight_packed,
+                                         const g4_f8e4m3* up_weight_scale,
+                                         const g4_f8e4m3* gate_weight_scale,
+                                         const g4_f8e4m3* down_weight_scale,
+                                         const float* up_global_scale, const float* gate_global_scale,
+                                         const float* down_global_scale,
+                                         const g4_bf16* post_ff_rms_weight, const g4_bf16* layer_scalar);
 
 /* All pages of one full-attention layer in ONE split-KV launch (replaces the host loop
  * of full_attention_first_page/_page dispatches, src/host/runtime.rs:438-459).

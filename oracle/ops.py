@@ -199,3 +199,100 @@ def final_norm_and_logits(x, rms_w, lm_head_bits: np.ndarray, rows_per_block: in
 
 def softcap(logits: np.ndarray) -> np.ndarray:
     return rb(np.tanh((np.asarray(logits, dtype=f32) / LOGIT_SOFTCAP).astype(f32)) * LOGIT_SOFTCAP)
+
+
+# ---------------------------------------------------------------------------- batched prefill
+# The reference prefills one position per dispatch (src/host/generate.rs:194-211) with
+# bf16 activations.  The library's batched prefill MLP (g4_decoder_feedforward_prefill)
+# feeds the block-scaled FP4 tensor cores, so it quantises each token's activations to
+# NVFP4 with the checkpoint weights' own recipe.  `prefill_feedforward` restates that
+# recipe around the reference MLP (decoder_feedforward above) so the CUDA path is checked
+# against exactly what it computes; the tests compare it with the unquantised reference as
+# well, to bound the quantisation's effect.
+
+def _nearest_code(v: np.ndarray, grid: np.ndarray) -> np.ndarray:
+    """Index of the nearest value of the ascending non-negative `grid` for v >= 0, ties
+    to the even index (round-to-nearest-even when consecutive codes alternate parity)."""
+    hi = np.clip(np.searchsorted(grid, v, side="left"), 1, len(grid) - 1)
+    lo = hi - 1
+    dlo, dhi = v - grid[lo], grid[hi] - v
+    pick_hi = (dhi < dlo) | ((dhi == dlo) & (hi % 2 == 0))
+    idx = np.where(pick_hi, hi, lo)
+    return np.where(v >= grid[-1], len(grid) - 1, idx)
+
+
+_E4M3_POS = prng.E4M3_VALUE[:127].astype(f32)  # codes 0x00..0x7E, ascending, 0..448
+
+
+def e4m3_round(v: np.ndarray) -> np.ndarray:
+    """Non-negative f32 -> nearest E4M3 value (ties to even, saturating at 448)."""
+    v = np.asarray(v, dtype=f32)
+    return _E4M3_POS[_nearest_code(np.minimum(v, f32(448.0)), _E4M3_POS)]
+
+
+def e2m1_round(v: np.ndarray) -> np.ndarray:
+    """f32 -> nearest E2M1 value (ties to even, saturating at +/-6)."""
+    v = np.asarray(v, dtype=f32)
+    mag = prng.E2M1_MAGNITUDE[_nearest_code(np.abs(v), prng.E2M1_MAGNITUDE)]
+    return np.where(v < 0, -mag, mag).astype(f32)
+
+
+def nvfp4_quantize_rows(x: np.ndarray, pieces: int = 1):
+    """Per row of x [T, K] (bf16 values), `pieces` NVFP4 rows sharing one scale
+    g = reciprocal(max|row|) * 2688: with y_0 = x * g,
+      s_p = e4m3(max_b|y_p| / 6)   (p = 0: e4m3(max_b|x| / 6 * g), the weight recipe),
+      c_p = e2m1(y_p / s_p),       y_{p+1} = y_p - c_p * s_p.
+    Returns the pieces' values the MMA sees, sum_p c_p * s_p (in f32), and 1/g per row
+    (0 for an all-zero row)."""
+    x = np.asarray(x, dtype=f32)
+    t, k = x.shape
+    amax = np.abs(x).max(axis=1)
+    zero = ~(amax > 0) | ~np.isfinite(amax)
+    safe = np.where(zero, f32(1.0), amax).astype(f32)
+    g = np.where(zero, f32(1.0), ((f32(1.0) / safe).astype(f32) * f32(2688.0)).astype(f32)).astype(f32)
+    blocks = x.reshape(t, k // 16, 16)
+    y = (blocks * g[:, None, None]).astype(f32)
+    smax = ((np.abs(blocks).max(axis=2) / f32(6.0)).astype(f32) * g[:, None]).astype(f32)
+    total = np.zeros_like(y)
+    for p in range(pieces):
+        if p > 0:
+            smax = (np.abs(y).max(axis=2) / f32(6.0)).astype(f32)
+        s = e4m3_round(smax)
+        s = np.where(zero[:, None], f32(0.0), s).astype(f32)
+        with np.errstate(divide="ignore", invalid="ignore"):
+            scaled = (y / s[:, :, None]).astype(f32)
+        piece = (np.where(s[:, :, None] > 0, e2m1_round(scaled), f32(0.0)) * s[:, :, None]).astype(f32)
+        y = (y - piece).astype(f32)
+        total = (total + piece).astype(f32)
+    ginv = np.where(zero, f32(0.0), (f32(1.0) / g).astype(f32)).astype(f32)
+    return total.reshape(t, k), ginv
+
+
+def prefill_feedforward(residual, pre_w, post_w, up_w, gate_w, down_w, up_gs, gate_gs, down_gs, layer_scalar,
+                        pieces: int = 2, world: int = 1):
+    """decoder_feedforward for T tokens [T, H] with activations as `pieces` NVFP4 pieces
+    (nvfp4_quantize_rows).  The weights are dequantised (nvfp4_dequant) f32 [rows, K];
+    global scales are the reciprocals the kernels take.  Rounding points as
+    decoder_feedforward, with x @ W.T replaced by (q(x) @ W.T) / g.  world > 1: the
+    tensor-parallel split, h quantised per rank's column slice and the ranks' down sums
+    (each divided by its own g) added in f32 before the bf16 roundings."""
+    res = np.asarray(residual, dtype=f32)
+    hidden = rms_norm(res, pre_w)
+    xq, gx = nvfp4_quantize_rows(hidden, pieces)
+
+    def proj(a, w, ginv, gs):
+        acc = (a @ w.T).astype(f32)
+        return rb(rb((acc * ginv[:, None]).astype(f32)) * f32(gs))
+
+    gate = proj(xq, gate_w, gx, gate_gs)
+    up = proj(xq, up_w, gx, up_gs)
+    act = rb(rb(gelu_tanh(gate)) * up)
+    lr = act.shape[1] // world
+    ysum = np.zeros((act.shape[0], down_w.shape[0]), dtype=f32)
+    for r in range(world):
+        hq, gh = nvfp4_quantize_rows(act[:, r * lr:(r + 1) * lr], pieces)
+        part = ((hq @ down_w[:, r * lr:(r + 1) * lr].T).astype(f32) * gh[:, None]).astype(f32)
+        ysum = (ysum + part).astype(f32)
+    down = rb(rb(ysum) * f32(down_gs))
+    hidden = rms_norm(down, post_w)
+    return rb(rb(res + hidden) * f32(layer_scalar))
