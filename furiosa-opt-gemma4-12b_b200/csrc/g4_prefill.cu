@@ -429,10 +429,9 @@ __device__ __forceinline__ uint32_t e4m3_byte(float v) {
   return s & 0xFFu;
 }
 
-constexpr int kQThreads = 256;
-constexpr int kMaxBlocksPerThread = 4;
+constexpr int kQThreads = 256;  // the tail kernel
 
-template <bool kMax>
+template <int T, bool kMax>
 __device__ __forceinline__ float block_reduce(float val, float* red) {
   val = kMax ? warp_max(val) : warp_sum(val);
   __syncthreads();
@@ -440,75 +439,103 @@ __device__ __forceinline__ float block_reduce(float val, float* red) {
   __syncthreads();
   float r = 0.f;
 #pragma unroll
-  for (int w = 0; w < kQThreads / 32; ++w) r = kMax ? fmaxf(r, red[w]) : r + red[w];
+  for (int w = 0; w < T / 32; ++w) r = kMax ? fmaxf(r, red[w]) : r + red[w];
   return r;
+}
+
+// y / s correctly rounded, given rcp = RN(1 / s): q0 = RN(y * rcp) is within an ulp of the
+// quotient, the remainder y - q0 * s is exact in one FMA, and one correction step gives
+// the correctly rounded quotient (Markstein's division theorem; the divisors here are
+// E4M3 values, the dividends normal f32 well inside the range).
+__device__ __forceinline__ float div_by(float y, float s, float rcp) {
+  const float q0 = __fmul_rn(y, rcp);
+  return __fmaf_rn(__fmaf_rn(-q0, s, y), rcp, q0);
 }
 
 // Per token: x (bf16 [K]; with norm_w, RMSNorm'ed and rounded to bf16 first) -> n_pieces
 // NVFP4 pieces (see the file comment): codes [piece][token][K/2] (low nibble first) at
 // piece stride code_pstride, scales [piece][token][scale_ld] at piece stride
 // scale_pstride, and 1/g.  A zero (or non-finite) row gets all codes and scales 0 and
-// 1/g = 0.  One CTA per token; thread b handles the 16-element blocks b, b + 256, ...
-__global__ void __launch_bounds__(kQThreads) pf_quant_kernel(const uint16_t* __restrict__ x, int K,
-                                                             const uint16_t* __restrict__ norm_w, int n_pieces,
-                                                             uint8_t* __restrict__ codes, size_t code_pstride,
-                                                             uint8_t* __restrict__ scales, int scale_ld,
-                                                             size_t scale_pstride, float* __restrict__ ginv) {
-  __shared__ float red[kQThreads / 32];
+// 1/g = 0.  One CTA of T threads per token; thread t handles the 16-element blocks
+// t, t + T, ... (at most NB of them), held as bf16 pairs in registers.
+template <int T, int NB>
+__global__ void __launch_bounds__(T, 768 / T) pf_quant_kernel(const uint16_t* __restrict__ x, int K,
+                                                     const uint16_t* __restrict__ norm_w, int n_pieces,
+                                                     uint8_t* __restrict__ codes, size_t code_pstride,
+                                                     uint8_t* __restrict__ scales, int scale_ld,
+                                                     size_t scale_pstride, float* __restrict__ ginv) {
+  __shared__ float red[T / 32];
   const int tok = blockIdx.x, tid = threadIdx.x;
   const int nb = K / 16;
   const uint16_t* row = x + static_cast<size_t>(tok) * K;
   pdl_wait();
-  float v[kMaxBlocksPerThread][16];
-  float ss = 0.f;
+  uint32_t w[NB][8];
 #pragma unroll
-  for (int i = 0; i < kMaxBlocksPerThread; ++i) {
-    const int b = tid + i * kQThreads;
+  for (int i = 0; i < NB; ++i) {
+    const int b = tid + i * T;
     if (b < nb) {
       const uint4 w0 = *reinterpret_cast<const uint4*>(row + 16 * b);
       const uint4 w1 = *reinterpret_cast<const uint4*>(row + 16 * b + 8);
-      const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      w[i][0] = w0.x, w[i][1] = w0.y, w[i][2] = w0.z, w[i][3] = w0.w;
+      w[i][4] = w1.x, w[i][5] = w1.y, w[i][6] = w1.z, w[i][7] = w1.w;
+    } else {
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        v[i][e] = bf16_to_f32(static_cast<uint16_t>((e & 1) ? ww[e >> 1] >> 16 : ww[e >> 1] & 0xFFFFu));
-        ss = __fadd_rn(ss, __fmul_rn(v[i][e], v[i][e]));
-      }
+      for (int e = 0; e < 8; ++e) w[i][e] = 0u;
     }
   }
+  auto lo = [](uint32_t v) { return bf16_to_f32(static_cast<uint16_t>(v & 0xFFFFu)); };
+  auto hi = [](uint32_t v) { return bf16_to_f32(static_cast<uint16_t>(v >> 16)); };
   if (norm_w != nullptr) {
-    const float r = rms_factor(block_reduce<false>(ss, red), K);
+    float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < kMaxBlocksPerThread; ++i) {
-      const int b = tid + i * kQThreads;
+    for (int i = 0; i < NB; ++i)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float a = lo(w[i][e]), c = hi(w[i][e]);
+        ss = __fadd_rn(ss, __fmul_rn(a, a));
+        ss = __fadd_rn(ss, __fmul_rn(c, c));
+      }
+    const float r = rms_factor(block_reduce<T, false>(ss, red), K);
+#pragma unroll
+    for (int i = 0; i < NB; ++i) {
+      const int b = tid + i * T;
       if (b < nb) {
+        const uint4 n0 = __ldg(reinterpret_cast<const uint4*>(norm_w + 16 * b));
+        const uint4 n1 = __ldg(reinterpret_cast<const uint4*>(norm_w + 16 * b + 8));
+        const uint32_t nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
 #pragma unroll
-        for (int e = 0; e < 16; ++e)
-          v[i][e] = round_bf16(__fmul_rn(__fmul_rn(v[i][e], r), bf16_to_f32(norm_w[16 * b + e])));
+        for (int e = 0; e < 8; ++e)
+          w[i][e] = pack_bf16x2(__fmul_rn(__fmul_rn(lo(w[i][e]), r), lo(nw[e])),
+                                __fmul_rn(__fmul_rn(hi(w[i][e]), r), hi(nw[e])));
       }
     }
   }
-  float bmax[kMaxBlocksPerThread], amax = 0.f;
+  // block maxima on the bf16 bit patterns (|x| orders like its low 15 bits)
+  uint32_t bm[NB], am = 0u;
 #pragma unroll
-  for (int i = 0; i < kMaxBlocksPerThread; ++i) {
-    bmax[i] = 0.f;
-    if (tid + i * kQThreads < nb) {
+  for (int i = 0; i < NB; ++i) {
+    uint32_t m2 = 0u;
 #pragma unroll
-      for (int e = 0; e < 16; ++e) bmax[i] = fmaxf(bmax[i], fabsf(v[i][e]));
-    }
-    amax = fmaxf(amax, bmax[i]);
+    for (int e = 0; e < 8; ++e) m2 = __vmaxu2(m2, w[i][e] & 0x7FFF7FFFu);
+    bm[i] = max(m2 & 0xFFFFu, m2 >> 16);
+    am = max(am, bm[i]);
   }
-  amax = block_reduce<true>(amax, red);
+  const float amax = block_reduce<T, true>(bf16_to_f32(static_cast<uint16_t>(am)), red);
   const bool zero = !(amax > 0.f) || !isfinite(amax);
   const float g = zero ? 1.0f : __fmul_rn(__frcp_rn(amax), 2688.0f);
   if (tid == 0) ginv[tok] = zero ? 0.f : __frcp_rn(g);
 #pragma unroll
-  for (int i = 0; i < kMaxBlocksPerThread; ++i) {
-    const int b = tid + i * kQThreads;
+  for (int i = 0; i < NB; ++i) {
+    const int b = tid + i * T;
     if (b >= nb) continue;
     float y[16];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) y[e] = __fmul_rn(v[i][e], g);
-    float smax = __fmul_rn(__fdiv_rn(bmax[i], 6.0f), g);  // piece 0: the weight recipe
+    for (int e = 0; e < 8; ++e) {
+      y[2 * e] = __fmul_rn(lo(w[i][e]), g);
+      y[2 * e + 1] = __fmul_rn(hi(w[i][e]), g);
+    }
+    // piece 0: the weight recipe, e4m3(max_b|x| / 6 * g)
+    float smax = __fmul_rn(__fdiv_rn(bf16_to_f32(static_cast<uint16_t>(bm[i])), 6.0f), g);
     for (int p = 0; p < n_pieces; ++p) {
       if (p > 0) {
         smax = 0.f;
@@ -519,16 +546,16 @@ __global__ void __launch_bounds__(kQThreads) pf_quant_kernel(const uint16_t* __r
       const uint32_t sc = zero ? 0u : e4m3_byte(fminf(smax, 448.0f));
       const float sf = e4m3_value(sc);
       uint32_t packed[2] = {0u, 0u};
+      if (sf > 0.f) {
+        const float rcp = __frcp_rn(sf);
 #pragma unroll
-      for (int e = 0; e < 16; e += 2) {
-        uint32_t two = 0u;
-        if (sf > 0.f) {
-          two = e2m1x2(__fdiv_rn(y[e], sf), __fdiv_rn(y[e + 1], sf));
+        for (int e = 0; e < 16; e += 2) {
+          const uint32_t two = e2m1x2(div_by(y[e], sf, rcp), div_by(y[e + 1], sf, rcp));
           const uint32_t hv = cvt_e2m1x2(two);  // the two code values, exact in f16
           y[e] = __fsub_rn(y[e], __fmul_rn(__half2float(__ushort_as_half(static_cast<uint16_t>(hv))), sf));
           y[e + 1] = __fsub_rn(y[e + 1], __fmul_rn(__half2float(__ushort_as_half(static_cast<uint16_t>(hv >> 16))), sf));
+          packed[e >> 3] |= two << (8 * ((e >> 1) & 3));
         }
-        packed[e >> 3] |= two << (8 * ((e >> 1) & 3));
       }
       *reinterpret_cast<uint2*>(codes + p * code_pstride + static_cast<size_t>(tok) * (K / 2) + 8 * b) =
           make_uint2(packed[0], packed[1]);
@@ -556,7 +583,7 @@ __global__ void __launch_bounds__(kQThreads) pf_tail_kernel(const float* __restr
     yv[i] = (c < H) ? round_bf16(__fmul_rn(round_bf16(y32[static_cast<size_t>(tok) * H + c]), gs)) : 0.f;
     ss = __fadd_rn(ss, __fmul_rn(yv[i], yv[i]));
   }
-  const float r = rms_factor(block_reduce<false>(ss, red), H);
+  const float r = rms_factor(block_reduce<kQThreads, false>(ss, red), H);
   const float ls = bf16_to_f32(layer_scalar[0]);
 #pragma unroll
   for (int i = 0; i < kPer; ++i) {
@@ -623,6 +650,17 @@ static g4_status launch_gemm(g4_ctx* ctx, CUtensorMap (&m)[6], const GemmArgs& g
   void* a[] = {&m[0], &m[1], &m[2], &m[3], &m[4], &m[5], &a_copy};
   return launch_kernel(ctx, fn, dim3(tiles < ctx->sm_count ? tiles : ctx->sm_count), dim3(kThreads), smem, a, false,
                        what);
+}
+// The quantiser instance for rows of nb 16-element blocks: T threads x NB blocks >= nb.
+static g4_status launch_quant(g4_ctx* ctx, int nb, int n, void** a, const char* what) {
+  const void* fn;
+  int threads = 128;
+  if (nb <= 128) fn = reinterpret_cast<const void*>(&pf_quant_kernel<128, 1>);
+  else if (nb <= 256) fn = reinterpret_cast<const void*>(&pf_quant_kernel<128, 2>);
+  else if (nb <= 512) fn = reinterpret_cast<const void*>(&pf_quant_kernel<128, 4>);
+  else if (nb <= 1024) fn = reinterpret_cast<const void*>(&pf_quant_kernel<256, 4>), threads = 256;
+  else return fail(ctx, G4_ERR_UNSUPPORTED, "prefill: row too long for the quantiser");
+  return launch_kernel(ctx, fn, dim3(n), dim3(threads), 0, a, false, what);
 }
 static g4_status launch_gemm_p(g4_ctx* ctx, int pieces, CUtensorMap (&m)[6], const GemmArgs& ga, const char* what) {
   switch (pieces) {
@@ -694,9 +732,7 @@ g4_status launch_prefill_feedforward(g4_ctx* ctx, int n, uint16_t* residual, con
     const uint16_t* x = residual;
     void* a[] = {(void*)&x,   (void*)&K,         (void*)&pre_w, (void*)&np,  (void*)&xq_codes,
                  (void*)&cps, (void*)&xq_scales, (void*)&sld,   (void*)&sps, (void*)&ginv_x};
-    if ((st = launch_kernel(ctx, (const void*)pf_quant_kernel, dim3(n), dim3(kQThreads), 0, a, false,
-                            "prefill norm+quant")) != G4_OK)
-      return st;
+    if ((st = launch_quant(ctx, H / 16, n, a, "prefill norm+quant")) != G4_OK) return st;
   }
   // 2. gate/up GEMM with the GeGLU epilogue -> h
   {
@@ -730,9 +766,7 @@ g4_status launch_prefill_feedforward(g4_ctx* ctx, int n, uint16_t* residual, con
     const uint16_t* nw = nullptr;
     void* a[] = {(void*)&x,   (void*)&K,         (void*)&nw,  (void*)&np,  (void*)&hq_codes,
                  (void*)&cps, (void*)&hq_scales, (void*)&sld, (void*)&sps, (void*)&ginv_h};
-    if ((st = launch_kernel(ctx, (const void*)pf_quant_kernel, dim3(n), dim3(kQThreads), 0, a, false,
-                            "prefill h quant")) != G4_OK)
-      return st;
+    if ((st = launch_quant(ctx, lrows / 16, n, a, "prefill h quant")) != G4_OK) return st;
   }
   // 4. down GEMM -> y (f32, this rank's k-slice)
   {
