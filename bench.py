@@ -119,6 +119,7 @@ class ClockSampler:
             time.sleep(self.period)
 
     def __enter__(self):
+        self._stop.clear()
         if self.ok:
             self._t = threading.Thread(target=self._run, daemon=True)
             self._t.start()
@@ -275,6 +276,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             decode = run_decode(args, ctx, stream, rank, world, dev)
         except Exception as e:  # the headline MLP line still prints
             decode = {"error": f"{type(e).__name__}: {e}"}
+    prefill = None
+    if not args.no_prefill:
+        try:
+            prefill = run_prefill(args, ctx, stream, rank, world, dev)
+        except Exception as e:  # the headline MLP line still prints
+            prefill = {"error": f"{type(e).__name__}: {e}"}
     vals = torch.tensor([total_ms / args.steps, kernel_ms, e2e_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
@@ -315,9 +322,35 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     }
     if decode is not None:
         line["decode"] = decode
+    if prefill is not None:
+        line["prefill"] = prefill
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args)
     return line
+
+
+def run_only(args, rank: int, world: int, local_rank: int) -> dict | None:
+    """One sub-measurement on its own (--only decode|prefill), printed as its own line."""
+    import torch
+
+    import g4b200 as g4
+
+    torch.cuda.set_device(local_rank)
+    dev = f"cuda:{local_rank}"
+    stream = torch.cuda.Stream(device=dev)
+    tpinfo = None
+    if world > 1:
+        import torch.distributed as dist
+
+        nid = [g4.Context.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(nid, src=0)
+        tpinfo = (rank, world, nid[0])
+    ctx = g4.Context(local_rank, stream=stream, tp=tpinfo)
+    try:
+        out = (run_decode if args.only == "decode" else run_prefill)(args, ctx, stream, rank, world, dev)
+    finally:
+        ctx.close()
+    return out if rank == 0 else None
 
 
 def _cpu_reference_tokens(steps: int, warmup: int, budget_s: float) -> tuple[float, int, int]:
@@ -437,6 +470,104 @@ def run_decode(args, ctx, stream, rank: int, world: int, dev: str) -> dict:
     }
 
 
+PREFILL_ORDER = ("pre_ff_rms_weight", "up_weight_packed", "gate_weight_packed", "down_weight_packed",
+                 "up_weight_scale", "gate_weight_scale", "down_weight_scale", "up_global_scale", "gate_global_scale",
+                 "down_global_scale", "post_ff_rms_weight", "layer_scalar")
+
+
+def run_prefill(args, ctx, stream, rank: int, world: int, dev: str) -> dict:
+    """the MLP block of M tokens at once (g4_decoder_feedforward_prefill)
+    on the block-scaled FP4 tensor cores, NVFP4 weights of config 1's distributions (seed
+    4), x ~ N(0, 1) bf16.  Timed per call with CUDA events (max over ranks), for the
+    default 2 activation pieces and for 1; e2e adds the residual's H2D copy from pinned
+    memory and its D2H read-back to every call."""
+    import torch
+    import torch.distributed as dist
+
+    import g4b200 as g4
+    from g4formats import quant, tp
+
+    M, reps = args.prefill_tokens, args.prefill_reps
+    m = quant.mlp_config1(seed=4, device=dev)
+    if world > 1:
+        m = tp.shard_mlp(m, rank, world)
+    w = [m[k] for k in PREFILL_ORDER]
+    g = torch.Generator(device=dev).manual_seed(4)
+    x0 = torch.randn(M, H, device=dev, generator=g).to(torch.bfloat16)
+    flops = 2.0 * M * H * L * 3
+    out = {}
+    sampler = ClockSampler(int(dev.split(":")[1]))
+    for pieces in (2, 1):
+        ctx.set_prefill_pieces(pieces)
+        r = x0.clone()
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                g4.decoder_feedforward_prefill(ctx, r, *w)
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with sampler, torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(reps):
+                g4.decoder_feedforward_prefill(ctx, r, *w)
+            e1.record(stream)
+            stream.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        # end to end: the residual from pinned host memory and back, every call
+        host_in = x0.cpu().pin_memory()
+        host_out = torch.empty_like(host_in).pin_memory()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(reps):
+                r.copy_(host_in, non_blocking=True)
+                g4.decoder_feedforward_prefill(ctx, r, *w)
+                host_out.copy_(r, non_blocking=True)
+            e1.record(stream)
+            stream.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / reps
+        vals = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        out[pieces] = vals.tolist()
+    ctx.set_prefill_pieces(2)
+    status = ctx.poll()
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    bf16 = float(peaks.get("bf16_tflops", 1590.0))
+    fp4_peak = 4.0 * bf16
+    ms2, e2e2 = out[2]
+    ms1, e2e1 = out[1]
+    tf2, tf1 = flops / (ms2 * 1e-3) / 1e12, flops / (ms1 * 1e-3) / 1e12
+    return {
+        "metric": "prefill MLP TFLOP/s", "value": round(tf2, 1), "unit": "TFLOP/s", "higher_is_better": True,
+        "n_gpus": world, "ms_per_call": round(ms2, 4), "dtype": "nvfp4 weights x nvfp4 activations (2 pieces), f32 acc",
+        "config": {"workload": "batched prefill MLP, BASELINE config 5 (M=4096 tokens, H=3840, L=15360, NVFP4 "
+                               "GeGLU block, tcgen05 kind::mxf4nvf4)", "tokens": M, "parallelism": f"tp{world}",
+                   "activation_pieces": 2, "flops_per_call": flops,
+                   "l2": "weights 99.5 MB + activations re-read from L2 across token tiles (one call per step)"},
+        "roofline": {"bound": "tensor", "achieved": round(tf2, 1), "peak": round(fp4_peak, 1), "unit": "TFLOP/s",
+                     "frac": round(tf2 / fp4_peak, 4),
+                     "peak_kind": "4 x measured bf16 cuBLAS burst (MEASURED_PEAKS.json bf16_tflops): the FP4 MMA "
+                                  "rate is 4x the bf16 rate; nominal dense FP4 9000",
+                     "tensor_work_factor": 2},
+        "one_piece": {"value": round(tf1, 1), "ms_per_call": round(ms1, 4), "frac": round(tf1 / fp4_peak, 4),
+                      "e2e_tflops": round(flops / (e2e1 * 1e-3) / 1e12, 1)},
+        "e2e": {"value": round(flops / (e2e2 * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "ms_per_call": round(e2e2, 4),
+                "h2d_bytes_per_step": M * H * 2, "d2h_bytes_per_step": M * H * 2,
+                "launch": "per call: pinned H2D copy of the residual, C-ABI call, D2H copy"},
+        "gpu_launches_per_call": 5 + (1 if world == 8 else 0),
+        "clocks": sampler.summary(), "device_status": status,
+    }
+
+
 def cpu_baseline(args) -> dict:
     """The reference's PyTorch CPU path (oracle port) on this host, bounded sample."""
     med, n, threads = _cpu_reference_tokens(args.steps, min(args.warmup, 5), args.cpu_budget)
@@ -478,6 +609,11 @@ def main() -> None:
     ap.add_argument("--no-decode", action="store_true", help="skip the whole-model decode measurement")
     ap.add_argument("--decode-context", type=int, default=4096)
     ap.add_argument("--decode-tokens", type=int, default=64)
+    ap.add_argument("--no-prefill", action="store_true", help="skip the batched prefill MLP measurement")
+    ap.add_argument("--prefill-tokens", type=int, default=4096)
+    ap.add_argument("--prefill-reps", type=int, default=30)
+    ap.add_argument("--only", choices=["decode", "prefill"], default=None,
+                    help="run just the whole-model decode or the prefill measurement (e.g. under a profiler)")
     ap.add_argument("--mlp-kernel", choices=["auto", "stream", "tensor"], default="auto",
                     help="decoder_feedforward kernel: streaming (CUDA-core decode) or tcgen05 (one GPU)")
     args = ap.parse_args()
@@ -502,7 +638,7 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device(f"cuda:{local_rank}"))
     try:
-        line = run_ours(args, rank, world, local_rank)
+        line = run_only(args, rank, world, local_rank) if args.only else run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -44,12 +44,19 @@ g4_status allow_max_dynamic_smem(g4_ctx* ctx, const void* fn, size_t need, const
 }
 
 g4_status launch_kernel(g4_ctx* ctx, const void* fn, dim3 grid, dim3 block, size_t smem, void** args,
-                        bool cooperative, const char* what) {
-  cudaLaunchAttribute attrs[2];
+                        bool cooperative, const char* what, unsigned cluster_x) {
+  cudaLaunchAttribute attrs[3];
   unsigned n = 0;
   if (cooperative) {
     attrs[n].id = cudaLaunchAttributeCooperative;
     attrs[n].val.cooperative = 1;
+    ++n;
+  }
+  if (cluster_x > 1) {
+    attrs[n].id = cudaLaunchAttributeClusterDimension;
+    attrs[n].val.clusterDim.x = cluster_x;
+    attrs[n].val.clusterDim.y = 1;
+    attrs[n].val.clusterDim.z = 1;
     ++n;
   }
   const unsigned base = n;
@@ -68,10 +75,11 @@ g4_status launch_kernel(g4_ctx* ctx, const void* fn, dim3 grid, dim3 block, size
   cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
   if (e != cudaSuccess && n > base) {
     (void)cudaGetLastError();
-    ctx->pdl_ok = false;
     cfg.numAttrs = base;
     e = cudaLaunchKernelExC(&cfg, fn, args);
+    if (e == cudaSuccess) ctx->pdl_ok = false;  // the launch attribute was what failed
   }
+  if (e != cudaSuccess) (void)cudaGetLastError();
   return check_cuda(ctx, e, what);
 }
 

@@ -13,6 +13,7 @@
 //      split-KV pass on the tensor cores (mma.sync, 16 q heads = the MMA's 16 rows), then a
 //      merge kernel; the row count may live in device memory so CUDA-graph replays follow
 //      the position.
+#include <cuda.h>
 #include <math_constants.h>
 
 #include "g4_internal.h"
@@ -612,6 +613,185 @@ __global__ void __launch_bounds__(kFaMergeThreads) fa_merge_kernel(const float* 
   if (quarter == 0 && tid == 0) running_sum[h] = 1.0f;
 }
 
+// ---------------------------------------------------------------------------- sliding, clustered
+// The 1024-slot ring of one KV head in ONE cluster of 8 CTAs: CTA r copies slots
+// [128 r, 128 r + 128) of K and V into shared memory with one TMA box each (the cache
+// viewed as [slot][kv head][256]: box 128 slots x 1 head x 256), computes its partial
+// softmax statistics and weighted V sum for the head's 2 q heads, and the cluster merges
+// the 8 partials through distributed shared memory (CTA r finishes dims [32 r, 32 r + 32)
+// of both heads, adding the partials in CTA order) -- no global round trip, no counter.
+// Same math as sliding_attn_kernel with 128-slot chunks.
+constexpr int kScRows = 128;
+constexpr int kScCtas = TS / kScRows;  // 8: the cluster
+constexpr int kScThreads = 256;
+
+struct __align__(128) ScSmem {  // TMA destinations: 128-byte aligned
+  uint16_t k[kScRows][DS];
+  uint16_t v[kScRows][DS];
+  float red[kScThreads / 32][GS][DS];
+  float q[GS][DS];
+  float o[GS][DS];  // this CTA's partial weighted sums (read by the cluster)
+  float s[GS][kScRows];
+  float valid[kScRows];
+  float m[GS], l[GS];
+  uint64_t full;
+};
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void tma_3d_load(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__global__ void __launch_bounds__(kScThreads) sliding_attn_cluster_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                                          const __grid_constant__ CUtensorMap vmap,
+                                                                          const uint16_t* q, const float* mask,
+                                                                          uint16_t* out, Scratch* scr,
+                                                                          uint64_t budget_ns) {
+  extern __shared__ uint8_t sc_raw[];
+  ScSmem& sm = *reinterpret_cast<ScSmem*>((reinterpret_cast<uintptr_t>(sc_raw) + 127) & ~uintptr_t(127));
+  const uint32_t r = cluster_ctarank();
+  const int h = blockIdx.x / kScCtas;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int row0 = static_cast<int>(r) * kScRows;
+  if (tid == 0) {
+    mbar_init(&sm.full, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_wait();  // q, the caches and the mask come from earlier kernels
+  const uint64_t deadline = global_ns() + budget_ns;
+  if (tid == 0) {
+    const uint64_t pol = l2_evict_first_policy();  // 335 MB of rings per token: streamed
+    mbar_arrive_expect_tx(&sm.full, 2u * kScRows * DS * 2u);
+    tma_3d_load(sm.k, &kmap, 0, h, row0, &sm.full, pol);
+    tma_3d_load(sm.v, &vmap, 0, h, row0, &sm.full, pol);
+  }
+  for (int i = tid; i < GS * DS; i += kScThreads)
+    sm.q[i / DS][i % DS] = bf16_to_f32(q[static_cast<size_t>(h) * GS * DS + i]);
+  if (tid < kScRows) sm.valid[tid] = mask[row0 + tid];
+  __syncthreads();
+  if (!mbar_wait(&sm.full, 0u, deadline)) atomicOr(&scr->status, DEV_ERR_TIMEOUT_MBAR);
+  pdl_launch_dependents();
+  // scores: warp w owns slots 16 w .. 16 w + 15, lane l dims 8 l .. 8 l + 7
+  float qa[8], qb[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    qa[i] = sm.q[0][8 * lane + i];
+    qb[i] = sm.q[1][8 * lane + i];
+  }
+#pragma unroll 4
+  for (int j = 0; j < 16; ++j) {
+    const int row = 16 * warp + j;
+    float kf[8];
+    bf16x8_to_f32(*reinterpret_cast<const uint4*>(&sm.k[row][8 * lane]), kf);
+    float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      d0 = fmaf(qa[i], kf[i], d0);
+      d1 = fmaf(qb[i], kf[i], d1);
+    }
+    d0 = warp_sum(d0);
+    d1 = warp_sum(d1);
+    if (lane == 0) {
+      const bool ok = sm.valid[row] > 0.f;
+      sm.s[0][row] = ok ? d0 : -CUDART_INF_F;
+      sm.s[1][row] = ok ? d1 : -CUDART_INF_F;
+    }
+  }
+  __syncthreads();
+  if (warp < GS) {
+    float e[4], mx = -CUDART_INF_F;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) mx = fmaxf(mx, sm.s[warp][lane + 32 * i]);
+    mx = warp_max(mx);
+    float l = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float a = sm.s[warp][lane + 32 * i];
+      e[i] = (a == -CUDART_INF_F) ? 0.f : expf(a - mx);
+      l += e[i];
+    }
+    l = warp_sum(l);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sm.s[warp][lane + 32 * i] = e[i];
+    if (lane == 0) {
+      sm.m[warp] = mx;
+      sm.l[warp] = l;
+    }
+  }
+  __syncthreads();
+  float o0[8], o1[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o0[i] = o1[i] = 0.f;
+#pragma unroll 4
+  for (int j = 0; j < 16; ++j) {
+    const int row = 16 * warp + j;
+    if (sm.valid[row] > 0.f) {  // unused ring slots may hold anything: never touched
+      float vf[8];
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(&sm.v[row][8 * lane]), vf);
+      const float p0 = sm.s[0][row], p1 = sm.s[1][row];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        o0[i] = fmaf(p0, vf[i], o0[i]);
+        o1[i] = fmaf(p1, vf[i], o1[i]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    sm.red[warp][0][8 * lane + i] = o0[i];
+    sm.red[warp][1][8 * lane + i] = o1[i];
+  }
+  __syncthreads();
+  for (int o = tid; o < GS * DS; o += kScThreads) {
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kScThreads / 32; ++w) acc += sm.red[w][o / DS][o % DS];
+    sm.o[o / DS][o % DS] = acc;
+  }
+  cluster_sync_all();  // every CTA's partial is complete and visible to the cluster
+  if (tid < GS * 32) {
+    const int hh = tid >> 5, d = 32 * static_cast<int>(r) + (tid & 31);
+    float mc[kScCtas], lc[kScCtas], oc[kScCtas], mx = -CUDART_INF_F;
+#pragma unroll
+    for (int c = 0; c < kScCtas; ++c) {
+      mc[c] = ld_cluster_f32(&sm.m[hh], static_cast<uint32_t>(c));
+      lc[c] = ld_cluster_f32(&sm.l[hh], static_cast<uint32_t>(c));
+      oc[c] = ld_cluster_f32(&sm.o[hh][d], static_cast<uint32_t>(c));
+      mx = fmaxf(mx, mc[c]);
+    }
+    float ls = 0.f, acc = 0.f;
+#pragma unroll
+    for (int c = 0; c < kScCtas; ++c) {
+      const float w = (mc[c] == -CUDART_INF_F) ? 0.f : expf(mc[c] - mx);
+      ls += w * lc[c];
+      acc += w * oc[c];
+    }
+    out[(static_cast<size_t>(h) * GS + hh) * DS + d] = f32_to_bf16(ls > 0.f ? acc / ls : 0.f);
+  }
+  cluster_sync_all();  // no CTA leaves while the others read its shared memory
+}
+
 // ---------------------------------------------------------------------------- launchers
 g4_status launch_full_page(g4_ctx* ctx, bool first, const uint16_t* q, const uint16_t* k, const uint16_t* v,
                            const float* mask, float* rmax, float* rsum, uint16_t* out) {
@@ -640,8 +820,49 @@ g4_status launch_gqa_attention(g4_ctx* ctx, const uint16_t* q, const uint16_t* k
                        false, "gqa attention");
 }
 
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+// The sliding cache [Ts][nkv][Ds] bf16 as a 3-D tensor (dims: Ds, nkv, Ts), box
+// 256 x 1 x 128: one CTA's 128 slots of one head.
+static bool cache_map(CUtensorMap* m, const void* base, int nkv) {
+  static EncodeFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    return (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+               ? reinterpret_cast<EncodeFn>(p)
+               : nullptr;
+  }();
+  if (fn == nullptr || !aligned16(base)) return false;
+  const cuuint64_t dims[3] = {DS, static_cast<cuuint64_t>(nkv), TS};
+  const cuuint64_t strides[2] = {DS * 2, static_cast<cuuint64_t>(nkv) * DS * 2};
+  const cuuint32_t box[3] = {DS, 1, kScRows};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The 1024-slot ring: one cluster of 8 CTAs per KV head (sliding_attn_cluster_kernel);
+// where the runtime refuses the cluster launch, the split-KV kernel with a global merge.
 g4_status launch_sliding_attention(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
                                    const float* mask, uint16_t* out) {
+  CUtensorMap km, vm;
+  const int nkv = NS / ctx->tp_world;
+  if (ctx->cluster_ok && cache_map(&km, k, nkv) && cache_map(&vm, v, nkv)) {
+    const void* fn = reinterpret_cast<const void*>(&sliding_attn_cluster_kernel);
+    const size_t smem = sizeof(ScSmem) + 128;
+    g4_status st = allow_max_dynamic_smem(ctx, fn, smem, "sliding attention");
+    if (st != G4_OK) return st;
+    Scratch* scr = ctx->buf.scratch;
+    uint64_t budget = ctx->wait_budget_ns;
+    void* args[] = {(void*)&km, (void*)&vm, (void*)&q, (void*)&mask, (void*)&out, (void*)&scr, (void*)&budget};
+    if (launch_kernel(ctx, fn, dim3(nkv * kScCtas), dim3(kScThreads), smem, args, false, "sliding attention",
+                      kScCtas) == G4_OK)
+      return G4_OK;
+    ctx->cluster_ok = false;  // not on this device / runtime: the split-KV kernel from now on
+  }
   return launch_gqa_attention(ctx, q, k, v, mask, TS, out);
 }
 

@@ -99,6 +99,7 @@ struct g4_ctx {
   std::string last_error;
   bool coop_ok = true;
   bool pdl_ok = true;  // programmatic dependent launch accepted by the runtime
+  bool cluster_ok = true;  // thread-block cluster launches accepted
   int mlp_kernel = 0;  // G4_MLP_AUTO / G4_MLP_STREAM / G4_MLP_TENSOR
   g4::PeerXch peers = {};  // TP exchange buffers mapped from every rank (world 0: NCCL path)
   g4::PrefillBuffers prefill;
@@ -145,7 +146,8 @@ g4_status allow_max_dynamic_smem(g4_ctx* ctx, const void* fn, size_t need, const
 // stream finishes, so it must execute griddepcontrol.wait before touching anything that
 // kernel wrote (weights, never written by these kernels, may be read before).  If the
 // runtime rejects that attribute once, the context launches without it from then on.
+// cluster_x > 1 launches clusters of that many CTAs along x.
 g4_status launch_kernel(g4_ctx* ctx, const void* fn, dim3 grid, dim3 block, size_t smem, void** args,
-                        bool cooperative, const char* what);
+                        bool cooperative, const char* what, unsigned cluster_x = 0);
 
 }  // namespace g4

@@ -56,7 +56,7 @@ constexpr uint32_t kIdesc = (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kTil
 
 template <int P>
 struct Cfg {
-  static constexpr int kStages = P == 1 ? 4 : (P == 2 ? 3 : 2);
+  static constexpr int kStages = P == 1 ? 6 : (P == 2 ? 4 : 3);  // 216 KB of ring each
   static constexpr uint32_t kStageTx = 16384 + 2048 + P * (16384 + 2048);
   static constexpr uint32_t kSfCols = 16 * (1 + P);  // TMEM scale columns per stage
   static_assert(kColSf + kStages * kSfCols <= kTmemCols, "tensor memory columns");
@@ -69,8 +69,8 @@ struct __align__(1024) Smem {
   uint8_t b[S][P][16384];        // token rows per piece, 128 x 128 B, 128-byte swizzle
   uint8_t sfa[S][2048];          // weight block scales [128][16 B]
   uint8_t sfb[S][P][2048];       // token block scales per piece [128][16 B]
-  uint16_t gate[kTile][66];      // gate/up epilogue (bf16 values): [token][intermediate row]
-  uint16_t up[kTile][66];
+  uint16_t gate[2][16][64];      // gate/up epilogue, 16 tokens at a time (double-buffered):
+  uint16_t up[2][16][64];        //   bf16 values [token][intermediate row]
   float ginv[kTile];             // this tile's per-token 1/g
   uint64_t full[S], sfready[S], empty[S];
   uint64_t dfull[2], dempty[2];
@@ -358,32 +358,50 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
       tc_fence_after();
       const uint32_t dcol = tbase + buf * kTile + ((32u * q) << 16);
       if (args.mode == 0) {
-        // accumulator rows 0..63 are gate rows, 64..127 the same intermediate rows' up
-        uint16_t(*dst)[66] = (m < 64) ? sm.gate : sm.up;
+        // Accumulator rows 0..63 are gate rows, 64..127 the same intermediate rows' up, so
+        // gate and up of one h meet in shared memory, 16 tokens at a time: every thread
+        // stores its row's 16 scaled values, then h = bf16(bf16(gelu(gate)) * up) for the
+        // chunk's 64 rows x 16 tokens, a warp writing 64 consecutive bf16 of one token.
+        // Chunks alternate buffers, so one barrier per chunk keeps writers behind readers.
         const float gs = (m < 64) ? gs_gate : gs_up;
         const int j = m & 63;
+        const int jp = etid & 31, r0 = etid >> 5;
+        uint16_t* hcol = args.h + static_cast<size_t>(64 * mt + 2 * jp);
+        // the whole row leaves tensor memory first, so the accumulator is free for the
+        // tile after next while the exchange runs
+        uint32_t hv[kTile / 2];
 #pragma unroll
         for (int c = 0; c < kTile / 16; ++c) {
           float v[16];
           tc_ld16(dcol + 16u * c, v);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) dst[16 * c + i][j] = f32_to_bf16(round_bf16(v[i] * sm.ginv[16 * c + i]) * gs);
+          for (int i = 0; i < 16; i += 2)
+            hv[8 * c + i / 2] = pack_bf16x2(round_bf16(v[i] * sm.ginv[16 * c + i]) * gs,
+                                            round_bf16(v[i + 1] * sm.ginv[16 * c + i + 1]) * gs);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.dempty[buf]);
-        named_bar_sync(kBarEpi, 128);
-        // h = bf16(bf16(gelu(gate)) * up): a warp writes 64 consecutive bf16 of one token
-        const int jp = etid & 31, r0 = etid >> 5;
-        uint16_t* hcol = args.h + static_cast<size_t>(64 * mt + 2 * jp);
-        for (int n = r0; n < kTile; n += 4) {
-          const int tok = kTile * nt + n;
-          if (tok >= args.n_tok) break;
-          const uint32_t g2 = *reinterpret_cast<const uint32_t*>(&sm.gate[n][2 * jp]);
-          const uint32_t u2 = *reinterpret_cast<const uint32_t*>(&sm.up[n][2 * jp]);
-          const float h0 = round_bf16(round_bf16(gelu_tanh(bf16_to_f32(g2 & 0xFFFFu))) * bf16_to_f32(u2 & 0xFFFFu));
-          const float h1 = round_bf16(round_bf16(gelu_tanh(bf16_to_f32(g2 >> 16))) * bf16_to_f32(u2 >> 16));
-          *reinterpret_cast<uint32_t*>(hcol + static_cast<size_t>(tok) * args.h_ld) = pack_bf16x2(h0, h1);
+#pragma unroll
+        for (int c = 0; c < kTile / 16; ++c) {
+          uint16_t(*dst)[64] = (m < 64) ? sm.gate[c & 1] : sm.up[c & 1];
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            dst[i][j] = static_cast<uint16_t>(hv[8 * c + i / 2] & 0xFFFFu);
+            dst[i + 1][j] = static_cast<uint16_t>(hv[8 * c + i / 2] >> 16);
+          }
+          named_bar_sync(kBarEpi, 128);
+#pragma unroll
+          for (int i = r0; i < 16; i += 4) {
+            const int tok = kTile * nt + 16 * c + i;
+            if (tok < args.n_tok) {
+              const uint32_t g2 = *reinterpret_cast<const uint32_t*>(&sm.gate[c & 1][i][2 * jp]);
+              const uint32_t u2 = *reinterpret_cast<const uint32_t*>(&sm.up[c & 1][i][2 * jp]);
+              const float h0 = round_bf16(round_bf16(gelu_tanh(bf16_to_f32(g2 & 0xFFFFu))) * bf16_to_f32(u2 & 0xFFFFu));
+              const float h1 = round_bf16(round_bf16(gelu_tanh(bf16_to_f32(g2 >> 16))) * bf16_to_f32(u2 >> 16));
+              *reinterpret_cast<uint32_t*>(hcol + static_cast<size_t>(tok) * args.h_ld) = pack_bf16x2(h0, h1);
+            }
+          }
         }
       } else {
         // y[token][row] = acc / g in f32 (the global scale and bf16 roundings follow the
@@ -643,6 +661,7 @@ template <int P>
 static g4_status launch_gemm(g4_ctx* ctx, CUtensorMap (&m)[6], const GemmArgs& ga, const char* what) {
   const void* fn = reinterpret_cast<const void*>(&pf_gemm_kernel<P>);
   const size_t smem = sizeof(Smem<P>) + 1024;
+  static_assert(sizeof(Smem<P>) + 1024 <= 232448, "shared memory per CTA");
   g4_status st = allow_max_dynamic_smem(ctx, fn, smem, what);
   if (st != G4_OK) return st;
   const int tiles = ga.m_tiles * ((ga.n_tok + kTile - 1) / kTile);

@@ -461,15 +461,24 @@ g4_status launch_qkv_fp8(g4_ctx*, bool, const uint16_t*, const uint8_t* const[3]
 g4_status launch_oproj_fp8(g4_ctx*, bool, const uint16_t*, const float*, const uint16_t*, const uint8_t*,
                            const uint16_t*, uint16_t*);
 
-// FP8 projections on one GPU run on the tensor-core GEMV of g4_fp8.cu unless
-// G4B200_PROJ_KERNEL=stream asks for the streaming engine (which also serves NVFP4 weights
-// and tensor-parallel contexts).
-static bool fp8_tensor_path(const g4_ctx* ctx) {
-  static const bool stream = [] {
+// FP8 projections on one GPU: project_qkv runs on the tensor-core GEMV of g4_fp8.cu, the
+// attention output on the streaming engine (its 240 or 480 row tiles spread over 148 SMs
+// more evenly there: 9 / 11 us against 12.5 / 20.7 us).  G4B200_PROJ_KERNEL=stream or
+// =tensor puts both on one kernel.  NVFP4 weights and tensor-parallel contexts always use
+// the streaming engine.
+static int proj_kernel_env() {
+  static const int kind = [] {
     const char* e = std::getenv("G4B200_PROJ_KERNEL");
-    return e != nullptr && std::strcmp(e, "stream") == 0;
+    if (e != nullptr && std::strcmp(e, "stream") == 0) return 1;
+    if (e != nullptr && std::strcmp(e, "tensor") == 0) return 2;
+    return 0;
   }();
-  return !stream && ctx->tp_world == 1;
+  return kind;
+}
+static bool fp8_tensor_path(const g4_ctx* ctx, bool oproj) {
+  if (ctx->tp_world != 1) return false;
+  const int kind = proj_kernel_env();
+  return kind == 2 || (kind == 0 && !oproj);
 }
 
 g4_status launch_qkv(g4_ctx* ctx, bool full, bool nvfp4, const uint16_t* x, const uint8_t* const w[3],
@@ -477,7 +486,7 @@ g4_status launch_qkv(g4_ctx* ctx, bool full, bool nvfp4, const uint16_t* x, cons
                      const uint16_t* in_w, const uint16_t* qn_w, const uint16_t* kn_w, const int32_t* kv_off,
                      const int32_t* rope_off, const uint16_t* cosT, const uint16_t* sinT, uint16_t* kcache,
                      uint16_t* vcache, uint16_t* q_out, long long cache_elems) {
-  if (!nvfp4 && fp8_tensor_path(ctx))
+  if (!nvfp4 && fp8_tensor_path(ctx, false))
     return launch_qkv_fp8(ctx, full, x, w, rs, in_w, qn_w, kn_w, kv_off, rope_off, cosT, sinT, kcache, vcache, q_out,
                           cache_elems);
   QkvOp op;
@@ -527,7 +536,7 @@ g4_status launch_qkv(g4_ctx* ctx, bool full, bool nvfp4, const uint16_t* x, cons
 g4_status launch_oproj(g4_ctx* ctx, bool full, bool nvfp4, const uint16_t* x, const float* rsum, const uint16_t* post_w,
                        const uint8_t* w, const uint8_t* bs, const uint16_t* row_scale, const float* gsc,
                        uint16_t* residual) {
-  if (!nvfp4 && fp8_tensor_path(ctx)) return launch_oproj_fp8(ctx, full, x, rsum, post_w, w, row_scale, residual);
+  if (!nvfp4 && fp8_tensor_path(ctx, true)) return launch_oproj_fp8(ctx, full, x, rsum, post_w, w, row_scale, residual);
   OprojOp op;
   const int tp = ctx->tp_world;
   op.K = (full ? QF : QS) / tp;
