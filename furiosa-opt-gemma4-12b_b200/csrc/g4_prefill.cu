@@ -163,6 +163,17 @@ __device__ __forceinline__ void write_sf(const uint8_t* rows16, uint32_t taddr, 
                           rw[0].z, rw[1].z, rw[2].z, rw[3].z, rw[0].w, rw[1].w, rw[2].w, rw[3].w};
   tc_st16(taddr, r);
 }
+// bf16 round-to-nearest-even with integer operations (the epilogue's conversions would
+// otherwise saturate the SM's conversion pipe, which also runs tanh): bit-identical to
+// cvt.rn.bf16.f32 for every finite value and infinity; a NaN stays a quiet NaN.
+__device__ __forceinline__ uint32_t bf16_rne_bits(float f) {
+  const uint32_t u = __float_as_uint(f);
+  const uint32_t r = (u + 0x7FFFu + ((u >> 16) & 1u)) >> 16;
+  return (f != f) ? ((u >> 16) | 0x40u) : r;
+}
+__device__ __forceinline__ float rne_bf16(float f) { return __uint_as_float(bf16_rne_bits(f) << 16); }
+__device__ __forceinline__ uint32_t pack_rne(float a, float b) { return bf16_rne_bits(a) | (bf16_rne_bits(b) << 16); }
+
 // bar.red.or over a named barrier: true on every participating thread if `pred` is true
 // on any (a decision all of them take together).
 __device__ __forceinline__ bool named_bar_any(uint32_t id, uint32_t threads, bool pred) {
@@ -376,8 +387,8 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
           tc_ld16(dcol + 16u * c, v);
 #pragma unroll
           for (int i = 0; i < 16; i += 2)
-            hv[8 * c + i / 2] = pack_bf16x2(round_bf16(v[i] * sm.ginv[16 * c + i]) * gs,
-                                            round_bf16(v[i + 1] * sm.ginv[16 * c + i + 1]) * gs);
+            hv[8 * c + i / 2] = pack_rne(rne_bf16(v[i] * sm.ginv[16 * c + i]) * gs,
+                                         rne_bf16(v[i + 1] * sm.ginv[16 * c + i + 1]) * gs);
         }
         tc_fence_before();
         __syncwarp();
@@ -397,9 +408,9 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
             if (tok < args.n_tok) {
               const uint32_t g2 = *reinterpret_cast<const uint32_t*>(&sm.gate[c & 1][i][2 * jp]);
               const uint32_t u2 = *reinterpret_cast<const uint32_t*>(&sm.up[c & 1][i][2 * jp]);
-              const float h0 = round_bf16(round_bf16(gelu_tanh(bf16_to_f32(g2 & 0xFFFFu))) * bf16_to_f32(u2 & 0xFFFFu));
-              const float h1 = round_bf16(round_bf16(gelu_tanh(bf16_to_f32(g2 >> 16))) * bf16_to_f32(u2 >> 16));
-              *reinterpret_cast<uint32_t*>(hcol + static_cast<size_t>(tok) * args.h_ld) = pack_bf16x2(h0, h1);
+              const float h0 = rne_bf16(gelu_tanh(__uint_as_float(g2 << 16))) * __uint_as_float(u2 << 16);
+              const float h1 = rne_bf16(gelu_tanh(__uint_as_float(g2 & 0xFFFF0000u))) * __uint_as_float(u2 & 0xFFFF0000u);
+              *reinterpret_cast<uint32_t*>(hcol + static_cast<size_t>(tok) * args.h_ld) = pack_rne(h0, h1);
             }
           }
         }
