@@ -1,3 +1,4 @@
+#include <cmath>
 // The C ABI of include/g4.h: argument validation and dispatch to the kernel launchers.
 #include <dlfcn.h>
 #include <nccl.h>
@@ -123,6 +124,14 @@ g4_status allreduce_f32(g4_ctx* ctx, float* buf, size_t count) {
   const ncclResult_t r =
       nccl().all_reduce(buf, buf, count, ncclFloat32, ncclSum, reinterpret_cast<ncclComm_t>(ctx->comm), ctx->stream);
   if (r != ncclSuccess) return fail(ctx, G4_ERR_NCCL, std::string("ncclAllReduce: ") + nccl().error_string(r));
+  return G4_OK;
+}
+
+g4_status allgather_u64n(g4_ctx* ctx, const uint64_t* in, uint64_t* out, int count) {
+  if (ctx->comm == nullptr || !nccl().ok) return fail(ctx, G4_ERR_NCCL, "tensor parallelism without a communicator");
+  const ncclResult_t r = nccl().all_gather(in, out, static_cast<size_t>(count), ncclUint64,
+                                           reinterpret_cast<ncclComm_t>(ctx->comm), ctx->stream);
+  if (r != ncclSuccess) return fail(ctx, G4_ERR_NCCL, std::string("ncclAllGather: ") + nccl().error_string(r));
   return G4_OK;
 }
 
@@ -283,6 +292,7 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   if (st == G4_OK) st = check_cuda(ctx, cudaMalloc(&b.tc_ptag, kTcPartWords * 8), "cudaMalloc tc_ptag");
   if (st == G4_OK) st = check_cuda(ctx, cudaMemset(b.tc_ptag, 0, kTcPartWords * 8), "cudaMemset tc_ptag");
   if (st == G4_OK) st = check_cuda(ctx, cudaMalloc(&b.tc_htag, kHFloats * 4), "cudaMalloc tc_htag");
+  if (st == G4_OK) st = check_cuda(ctx, cudaMalloc(&b.cand, kCandWords * 8), "cudaMalloc cand");
   if (st == G4_OK) st = check_cuda(ctx, cudaMemset(b.tc_htag, 0, kHFloats * 4), "cudaMemset tc_htag");
   if (st == G4_OK) st = check_cuda(ctx, cudaDeviceSynchronize(), "ctx init");
   if (st != G4_OK) {
@@ -308,6 +318,7 @@ g4_status g4_ctx_destroy(g4_ctx* ctx) {
   cudaFree(ctx->buf.tc_seg);
   cudaFree(ctx->buf.tc_ptag);
   cudaFree(ctx->buf.tc_htag);
+  cudaFree(ctx->buf.cand);
   cudaFree(ctx->prefill.xq);
   cudaFree(ctx->prefill.h);
   cudaFree(ctx->prefill.hq);
@@ -614,6 +625,21 @@ g4_status g4_final_norm_and_logits(g4_ctx* ctx, const g4_bf16* input, const g4_b
   G4_CHECK_CTX(ctx);
   G4_REQUIRE_PTRS(ctx, input, rms_weight, lm_head_weight, out);
   return launch_lm_head(ctx, input, rms_weight, lm_head_weight, out);
+}
+
+g4_status g4_sample_top_k_top_p(g4_ctx* ctx, const g4_bf16* logits, int n, float temperature, int top_k,
+                                float top_p, const int32_t* banned, int n_banned, const float* uniform,
+                                int32_t* out_index) {
+  G4_CHECK_CTX(ctx);
+  G4_REQUIRE_PTRS(ctx, logits);
+  G4_REQUIRE_SCALARS(ctx, uniform, out_index);
+  if (n <= 0 || n > 262144) return fail(ctx, G4_ERR_BAD_ARG, "n must be in [1, 262144]");
+  if (top_k < 1 || n_banned < 0 || top_k + n_banned > 128)
+    return fail(ctx, G4_ERR_BAD_ARG, "need top_k >= 1 and top_k + n_banned <= 128");
+  if (n_banned > 0 && banned == nullptr) return fail(ctx, G4_ERR_BAD_ARG, "banned is null");
+  if (!(top_p > 0.f) || !(top_p <= 1.f)) return fail(ctx, G4_ERR_BAD_ARG, "top_p must be in (0, 1]");
+  if (!(temperature >= 0.f) || !std::isfinite(temperature)) return fail(ctx, G4_ERR_BAD_ARG, "bad temperature");
+  return launch_sample(ctx, logits, n, temperature, top_k, top_p, banned, n_banned, uniform, out_index);
 }
 
 g4_status g4_argmax_bf16(g4_ctx* ctx, const g4_bf16* logits, int n, int32_t* out_index) {

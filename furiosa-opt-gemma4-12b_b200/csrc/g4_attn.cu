@@ -615,8 +615,8 @@ __global__ void __launch_bounds__(kFaMergeThreads) fa_merge_kernel(const float* 
 
 // ---------------------------------------------------------------------------- sliding, clustered
 // The 1024-slot ring of one KV head in ONE cluster of 8 CTAs: CTA r copies slots
-// [128 r, 128 r + 128) of K and V into shared memory with one TMA box each (the cache
-// viewed as [slot][kv head][256]: box 128 slots x 1 head x 256), computes its partial
+// [128 r, 128 r + 128) of K and V into shared memory as 16 TMA boxes each (the cache
+// viewed as [slot][kv head][256]: box 8 slots x 1 head x 256), computes its partial
 // softmax statistics and weighted V sum for the head's 2 q heads, and the cluster merges
 // the 8 partials through distributed shared memory (CTA r finishes dims [32 r, 32 r + 32)
 // of both heads, adding the partials in CTA order) -- no global round trip, no counter.
@@ -624,6 +624,7 @@ __global__ void __launch_bounds__(kFaMergeThreads) fa_merge_kernel(const float* 
 constexpr int kScRows = 128;
 constexpr int kScCtas = TS / kScRows;  // 8: the cluster
 constexpr int kScThreads = 256;
+constexpr int kScBox = kScRows / 16;   // slots per TMA box
 
 struct __align__(128) ScSmem {  // TMA destinations: 128-byte aligned
   uint16_t k[kScRows][DS];
@@ -680,11 +681,16 @@ __global__ void __launch_bounds__(kScThreads) sliding_attn_cluster_kernel(const 
   __syncthreads();
   pdl_wait();  // q, the caches and the mask come from earlier kernels
   const uint64_t deadline = global_ns() + budget_ns;
-  if (tid == 0) {
+  if (warp == 0) {
+    // 16 boxes of 8 slots per tensor, one per lane: many copies in flight at once
     const uint64_t pol = l2_evict_first_policy();  // 335 MB of rings per token: streamed
-    mbar_arrive_expect_tx(&sm.full, 2u * kScRows * DS * 2u);
-    tma_3d_load(sm.k, &kmap, 0, h, row0, &sm.full, pol);
-    tma_3d_load(sm.v, &vmap, 0, h, row0, &sm.full, pol);
+    if (lane == 0) mbar_arrive_expect_tx(&sm.full, 2u * kScRows * DS * 2u);
+    __syncwarp();
+    const int b = lane & 15;
+    if (lane < 16)
+      tma_3d_load(sm.k[kScBox * b], &kmap, 0, h, row0 + kScBox * b, &sm.full, pol);
+    else
+      tma_3d_load(sm.v[kScBox * b], &vmap, 0, h, row0 + kScBox * b, &sm.full, pol);
   }
   for (int i = tid; i < GS * DS; i += kScThreads)
     sm.q[i / DS][i % DS] = bf16_to_f32(q[static_cast<size_t>(h) * GS * DS + i]);
@@ -824,7 +830,7 @@ using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, voi
                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                               CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 // The sliding cache [Ts][nkv][Ds] bf16 as a 3-D tensor (dims: Ds, nkv, Ts), box
-// 256 x 1 x 128: one CTA's 128 slots of one head.
+// 256 x 1 x 8: 8 slots of one head (a CTA's 128 slots are 16 boxes).
 static bool cache_map(CUtensorMap* m, const void* base, int nkv) {
   static EncodeFn fn = [] {
     void* p = nullptr;
@@ -837,7 +843,7 @@ static bool cache_map(CUtensorMap* m, const void* base, int nkv) {
   if (fn == nullptr || !aligned16(base)) return false;
   const cuuint64_t dims[3] = {DS, static_cast<cuuint64_t>(nkv), TS};
   const cuuint64_t strides[2] = {DS * 2, static_cast<cuuint64_t>(nkv) * DS * 2};
-  const cuuint32_t box[3] = {DS, 1, kScRows};
+  const cuuint32_t box[3] = {DS, 1, kScBox};
   const cuuint32_t estr[3] = {1, 1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

@@ -38,6 +38,7 @@ constexpr size_t kAttnFloats = 512 * (2 * 16 + 16 * 512) + 4096;  // 512 chunks 
 constexpr size_t kTcTiles = 15360 / 64 + 3840 / 128;              // gate/up tiles + down tiles
 constexpr size_t kTcSegFloats = 3840;                             // the down projection's H sums
 constexpr size_t kTcPartWords = kTcTiles * 8 * 128;                // tagged segment partials (both phases)
+constexpr size_t kCandWords = 16384 + 128 + 8 * 128;              // sampling: candidates, a rank's share, gathered
 
 // Tensor-parallel one-shot all-reduce over peer memory.  Each rank owns one exchange
 // buffer of 64-bit words, word[2][kMaxTp][3840]: two halves used by alternate launches,
@@ -69,6 +70,7 @@ struct DeviceBuffers {
   // wrote it (zero at creation): segment partials {f32, tag} and h {bf16, tag}.
   uint64_t* tc_ptag = nullptr;  // [kTcPartWords]
   uint32_t* tc_htag = nullptr;  // [kHFloats]
+  uint64_t* cand = nullptr;     // [kCandWords] sampling candidates (g4_sample.cu)
 };
 
 // Batched prefill feed-forward scratch, grown to the largest token count seen and kept
@@ -123,6 +125,11 @@ g4_status allreduce_f32(g4_ctx* ctx, float* buf, size_t count);
 void model_adopt(g4_model* model, const std::vector<void*>& ptrs, int device);
 // Every rank's one 64-bit word into out[world] (NCCL all-gather on the context's stream).
 g4_status allgather_u64(g4_ctx* ctx, const uint64_t* in, uint64_t* out);
+// Every rank's `count` 64-bit words into out[world][count].
+g4_status allgather_u64n(g4_ctx* ctx, const uint64_t* in, uint64_t* out, int count);
+// Top-k / top-p sampling of this rank's logits[n] (g4_sample.cu).
+g4_status launch_sample(g4_ctx* ctx, const uint16_t* logits, int n, float temperature, int top_k, float top_p,
+                        const int32_t* banned, int n_banned, const float* uniform, int32_t* out_index);
 bool mlp_tc_enabled(const g4_ctx* ctx);
 g4_status launch_decoder_feedforward_tc(g4_ctx* ctx, uint16_t* residual, const uint16_t* pre_w,
                                         const uint8_t* up_p, const uint8_t* gate_p, const uint8_t* down_p,

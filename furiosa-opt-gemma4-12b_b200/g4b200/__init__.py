@@ -237,6 +237,7 @@ for _n, _k in [("g4_embed_token", 3), ("g4_copy_hidden_state", 2), ("g4_sliding_
     _declare(_n, _k)
 LIB.g4_full_attention_paged.argtypes = [_vp, _vp, _vp, _vp, _i32, _i32, _vp, _vp]
 LIB.g4_argmax_bf16.argtypes = [_vp, _vp, _i32, _vp]
+LIB.g4_sample_top_k_top_p.argtypes = [_vp, _vp, _i32, ctypes.c_float, _i32, ctypes.c_float, _vp, _i32, _vp, _vp]
 LIB.g4_attention_gqa.argtypes = [_vp, _vp, _vp, _vp, _vp, _i32, _vp]
 LIB.g4_dequant_nvfp4.argtypes = [_vp, _vp, _vp, _i32, _i32, _vp]
 LIB.g4_dequant_fp8.argtypes = [_vp, _vp, _i64, _vp]
@@ -519,6 +520,23 @@ def decoder_feedforward(ctx: Context, residual, pre_ff_rms_weight, up_weight_pac
     ctx.call("g4_decoder_feedforward", residual, pre_ff_rms_weight, up_weight_packed, gate_weight_packed,
              down_weight_packed, up_weight_scale, gate_weight_scale, down_weight_scale, up_global_scale,
              gate_global_scale, down_global_scale, post_ff_rms_weight, layer_scalar)
+
+
+def sample_top_k_top_p(ctx: Context, logits, temperature: float, top_k: int, top_p: float, banned, uniform,
+                       out_index) -> None:
+    """Top-k / top-p sampling of logits (bf16 [n]; TP: the rank's vocab slice) on the device
+    (g4_sample_top_k_top_p, src/host/sampling.rs:20-72).  `banned`: distinct token ids
+    (a host sequence); `uniform`: a float32 CUDA tensor holding the draw in [0, 1);
+    `out_index`: an int32 CUDA tensor of one element."""
+    t = _t()
+    _expect("logits", logits, None, (t.bfloat16,))
+    _expect("uniform", uniform, 1, (t.float32,))
+    _expect("out_index", out_index, 1, (t.int32,))
+    ids = list(banned)
+    arr = (ctypes.c_int32 * max(1, len(ids)))(*ids)
+    ctx._check("g4_sample_top_k_top_p", LIB.g4_sample_top_k_top_p(
+        ctx.handle, _ptr(logits), logits.numel(), float(temperature), int(top_k), float(top_p),
+        ctypes.cast(arr, _vp), len(ids), _ptr(uniform), _ptr(out_index)))
 
 
 PREFILL_MAX_TOKENS = 65536

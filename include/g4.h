@@ -270,6 +270,19 @@ g4_status g4_full_attention_paged(g4_ctx* ctx, const g4_bf16* q, const g4_bf16* 
  * of logits[n] (bf16). */
 g4_status g4_argmax_bf16(g4_ctx* ctx, const g4_bf16* logits, int n, int32_t* out_index);
 
+/* Top-k / top-p sampling on the device (src/host/sampling.rs:20-72; replaces the
+ * logits read-back and host sampling of src/host/generate.rs:135-143): keep the
+ * (top_k + n_banned) largest logits, drop the `banned` ids (distinct; host array) unless
+ * that drops all, keep top_k, p = softmax((l - l_max) / max(temperature, 1e-5)), the
+ * nucleus = the shortest prefix whose running sum reaches top_p, and *out_index = the
+ * first id whose running sum reaches (*uniform) x (nucleus sum).  `uniform` is a device
+ * f32 in [0, 1) (the host's draw).  Equal logits rank by lower id.  1 <= top_k,
+ * top_k + n_banned <= 128, 0 < top_p <= 1.  TP: logits is the rank's vocab slice of n
+ * entries (ids rank*n ...); every rank gets the same id. */
+g4_status g4_sample_top_k_top_p(g4_ctx* ctx, const g4_bf16* logits, int n, float temperature, int top_k,
+                                float top_p, const int32_t* banned, int n_banned, const float* uniform,
+                                int32_t* out_index);
+
 /* Bit-exact dequantisation checks (scripts/generate_references.py:207-216,622-626):
  * out[n,k] = bf16(e2m1(codes) * e4m3(scale[n, k/16])) and out[n,k] = bf16(e4m3(w)). */
 g4_status g4_dequant_nvfp4(g4_ctx* ctx, const g4_f4x2* packed, const g4_f8e4m3* block_scale,

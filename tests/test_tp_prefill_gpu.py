@@ -1,11 +1,13 @@
-"""Tensor-parallel batched prefill (g4_decoder_feedforward_prefill) on 2, 4 or 8 GPUs,
-ranks as child processes.  Each rank holds its gate/up rows and its down k-slice (8-way:
+"""Tensor-parallel batched prefill (g4_decoder_feedforward_prefill) and sampling
+(g4_sample_top_k_top_p) on 2, 4 or 8 GPUs, ranks as child processes.  Each rank holds its gate/up rows and its down k-slice (8-way:
 120-byte scale rows, which the library re-lays out for TMA), quantises its own slice of
 h, and the ranks' f32 down sums are all-reduced over NCCL before the tail.
 
   * every rank ends with the same residual, bit for bit;
   * rank 0's result matches oracle/ops.py:prefill_feedforward with the same tensor-parallel
-    split (h quantised per rank slice) within the single-GPU prefill tolerance.
+    split (h quantised per rank slice) within the single-GPU prefill tolerance;
+  * sampling over vocab slices: every rank draws the same id, the oracle's on the whole
+    vocabulary (the ranks' top-k candidates are all-gathered).
 
 NVLS is off (NCCL_NVLS_ENABLE=0).  Skipped with fewer GPUs than ranks.
 """
@@ -78,6 +80,30 @@ def _rank(rank: int, world: int, port: int, q) -> None:
             base = f(r0)
             a, b = want - base, f(r) - base
             res["rel_l2"] = float(np.linalg.norm(a - b) / np.linalg.norm(a))
+        # sampling: the rank's vocab slice, the same draw everywhere
+        from oracle import prng
+        from oracle import sampling as smp
+
+        W = 262144
+        xs = np.tanh(np.random.default_rng(9).standard_normal(W).astype(np.float32) * 0.1) * 30.0
+        bits = prng.bf16_bits(xs.astype(np.float32)).astype(np.uint16)
+        sl = W // world
+        mine = torch.from_numpy(bits[rank * sl:(rank + 1) * sl].view(np.int16).copy()).view(torch.bfloat16).cuda()
+        u = torch.zeros(1, dtype=torch.float32, device="cuda")
+        out = torch.zeros(1, dtype=torch.int32, device="cuda")
+        picks, want = [], []
+        for uu in (0.0, 0.3, 0.77, 0.99):
+            u.fill_(uu)
+            g4.sample_top_k_top_p(ctx, mine, 1.0, 64, 0.95, [5, 7], u, out)
+            torch.cuda.synchronize()
+            picks.append(int(out.item()))
+            want.append(smp.sample(bits, 1.0, 64, 0.95, [5, 7], uu))
+        t = torch.tensor(picks, dtype=torch.int32, device="cuda")
+        ts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(ts, t)
+        res["sample_identical"] = all(torch.equal(ts[0], x) for x in ts)
+        res["sample_picks"] = picks
+        res["sample_want"] = want
         dist.barrier()
         ctx.close()
     finally:
@@ -108,3 +134,5 @@ def test_tensor_parallel_prefill(world):
     print(f"TP{world} prefill: ranks identical {res['identical']}, contribution rel-L2 {res['rel_l2']:.3e}")
     assert res["identical"], res
     assert res["rel_l2"] <= PREFILL_REL_L2, res
+    assert res["sample_identical"], res
+    assert res["sample_picks"] == res["sample_want"], res
