@@ -128,8 +128,11 @@ g4_status allgather_u64(g4_ctx* ctx, const uint64_t* in, uint64_t* out);
 // Every rank's `count` 64-bit words into out[world][count].
 g4_status allgather_u64n(g4_ctx* ctx, const uint64_t* in, uint64_t* out, int count);
 // Top-k / top-p sampling of this rank's logits[n] (g4_sample.cu).
+// draw_pos non-null: the draw is derived on the device from (seed, *draw_pos) instead of
+// read from `uniform` (the decode runtime's per-position draw).
 g4_status launch_sample(g4_ctx* ctx, const uint16_t* logits, int n, float temperature, int top_k, float top_p,
-                        const int32_t* banned, int n_banned, const float* uniform, int32_t* out_index);
+                        const int32_t* banned, int n_banned, const float* uniform, int32_t* out_index,
+                        const int32_t* draw_pos = nullptr, uint64_t seed = 0);
 bool mlp_tc_enabled(const g4_ctx* ctx);
 g4_status launch_decoder_feedforward_tc(g4_ctx* ctx, uint16_t* residual, const uint16_t* pre_w,
                                         const uint8_t* up_p, const uint8_t* gate_p, const uint8_t* down_p,

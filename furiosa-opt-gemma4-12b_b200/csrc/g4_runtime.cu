@@ -233,6 +233,15 @@ __global__ void __launch_bounds__(256) argmax_step_kernel(const uint16_t* logits
   }
 }
 
+// Top-k / top-p mode: the sampled token (every rank drew the same) finishes the step.
+__global__ void sample_finish_kernel(const int32_t* picked, StepState* st, const int32_t* prompt,
+                                     int32_t* generated, int32_t* pred_log, int max_pos) {
+  pdl_wait();
+  if (threadIdx.x != 0) return;
+  const uint64_t key = 0xFFFFFFFFu - static_cast<uint32_t>(*picked);  // finish_step's key of `picked`
+  finish_step(st, key, prompt, generated, pred_log, max_pos);
+}
+
 __global__ void step_finish_kernel(const uint64_t* gathered, int world, StepState* st, const int32_t* prompt,
                                    int32_t* generated, int32_t* pred_log, int max_pos) {
   pdl_wait();
@@ -303,6 +312,12 @@ struct g4_workspace {
   uint16_t* logits = nullptr;
   uint64_t* cand = nullptr;  // [kArgmaxCtas] candidates, then [kMaxTp] gather in/out
   uint32_t* ticket = nullptr;
+  int32_t* picked = nullptr;  // the sampled token of the step (top-k / top-p mode)
+  // sampling (g4_workspace_set_sampling): top_k == 0 is greedy
+  int sample_k = 0;
+  float sample_t = 1.0f, sample_p = 1.0f;
+  std::vector<int32_t> sample_banned;
+  uint64_t sample_seed = 0;
   std::vector<void*> allocs;
   cudaGraphExec_t exec = nullptr;
   const g4_model* graph_model = nullptr;
@@ -407,6 +422,16 @@ g4_status issue_step(g4_ctx* ctx, g4_workspace* ws, const g4_model* m) {
   s = launch_lm_head(ctx, ws->x, static_cast<const uint16_t*>(m->final_norm.ptr),
                      embed + static_cast<size_t>(ws->rank) * vrows * H, ws->logits);
   if (s != G4_OK) return s;
+  if (ws->sample_k > 0) {
+    // top-k / top-p with the step's own draw (seed, position), then the step advance
+    s = launch_sample(ctx, ws->logits, vrows, ws->sample_t, ws->sample_k, ws->sample_p, ws->sample_banned.data(),
+                      static_cast<int>(ws->sample_banned.size()), nullptr, ws->picked, &st->pos, ws->sample_seed);
+    if (s != G4_OK) return s;
+    int maxp = ws->max_pos;
+    void* b[] = {(void*)&ws->picked, (void*)&st, (void*)&ws->prompt, (void*)&ws->generated, (void*)&ws->pred_log,
+                 (void*)&maxp};
+    return launch_kernel(ctx, (const void*)sample_finish_kernel, dim3(1), dim3(32), 0, b, false, "sample finish");
+  }
   {
     const uint16_t* lg = ws->logits;
     int n = vrows, world = ws->world, maxp = ws->max_pos;
@@ -592,6 +617,7 @@ g4_status g4_workspace_create(g4_ctx* ctx, const g4_model* m, int max_positions,
   alloc((void**)&ws->logits, static_cast<size_t>(W / ws->world) * 2, "logits");
   alloc((void**)&ws->cand, (kArgmaxCtas + 2 * kMaxTp) * 8, "argmax candidates");
   alloc((void**)&ws->ticket, 4, "argmax ticket");
+  alloc((void**)&ws->picked, 4, "sampled token");
   if (s == G4_OK) {
     std::vector<uint16_t> c, sn;
     rope_data(DS, 10000.0f, DS, c, sn);  // runtime.rs:153
@@ -610,6 +636,25 @@ g4_status g4_workspace_create(g4_ctx* ctx, const g4_model* m, int max_positions,
     return s;
   }
   *out = ws;
+  return G4_OK;
+}
+
+g4_status g4_workspace_set_sampling(g4_workspace* ws, float temperature, int top_k, float top_p,
+                                    const int32_t* banned, int n_banned, uint64_t seed) {
+  if (ws == nullptr) return G4_ERR_BAD_ARG;
+  if (top_k < 0 || n_banned < 0 || top_k + n_banned > 128 || (n_banned > 0 && banned == nullptr)) return G4_ERR_BAD_ARG;
+  if (top_k > 0 && (!(top_p > 0.f) || !(top_p <= 1.f) || !(temperature >= 0.f) || !std::isfinite(temperature)))
+    return G4_ERR_BAD_ARG;
+  ws->sample_k = top_k;
+  ws->sample_t = temperature;
+  ws->sample_p = top_p;
+  ws->sample_banned.assign(banned, banned + n_banned);
+  ws->sample_seed = seed;
+  if (ws->exec != nullptr) {  // the step graph changes: capture it again on next use
+    cudaSetDevice(ws->device);
+    cudaGraphExecDestroy(ws->exec);
+    ws->exec = nullptr;
+  }
   return G4_OK;
 }
 

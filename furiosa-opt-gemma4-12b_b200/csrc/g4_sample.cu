@@ -72,6 +72,17 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(const uint16_t* __r
   for (int i = threadIdx.x; i < kk; i += kSelThreads) cand[static_cast<size_t>(blockIdx.x) * kk + i] = keys[i];
 }
 
+// The decode runtime's draw for the step at `pos`: splitmix64 of seed + pos * golden
+// ratio, top 24 bits as a float in [0, 1) (the same construction as a uniform f32 from
+// 24 random bits; reproducible on the host).
+__device__ __forceinline__ float draw_uniform(uint64_t seed, int pos) {
+  uint64_t z = seed + static_cast<uint64_t>(static_cast<uint32_t>(pos)) * 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return static_cast<float>(z >> 40) * (1.0f / 16777216.0f);
+}
+
 struct SampleArgs {
   int m;           // candidate keys
   int kk;          // top_k + banned (kept before filtering)
@@ -81,6 +92,8 @@ struct SampleArgs {
   float temperature;
   float top_p;
   int reduce;      // 1: write the top kk keys to out_keys (a rank's share), 0: sample
+  const int32_t* draw_pos;  // non-null: u = draw_uniform(seed, *draw_pos) instead of *uniform
+  uint64_t seed;
 };
 
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const uint64_t* __restrict__ cand,
@@ -140,7 +153,8 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const uint64_t* 
   }
   float nsum = 0.f;
   for (int i = 0; i < nucleus; ++i) nsum = __fadd_rn(nsum, p[i]);
-  const float threshold = __fmul_rn(*uniform, nsum);
+  const float u = a.draw_pos != nullptr ? draw_uniform(a.seed, *a.draw_pos) : *uniform;
+  const float threshold = __fmul_rn(u, nsum);
   int pick = ids[nucleus - 1];
   float acc = 0.f;
   for (int i = 0; i < nucleus; ++i) {
@@ -156,7 +170,8 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const uint64_t* 
 }  // namespace smp
 
 g4_status launch_sample(g4_ctx* ctx, const uint16_t* logits, int n, float temperature, int top_k, float top_p,
-                        const int32_t* banned, int n_banned, const float* uniform, int32_t* out_index) {
+                        const int32_t* banned, int n_banned, const float* uniform, int32_t* out_index,
+                        const int32_t* draw_pos, uint64_t seed) {
   using namespace smp;
   const int kk = top_k + n_banned < n * ctx->tp_world ? top_k + n_banned : n * ctx->tp_world;
   const int grid = (n + kChunk - 1) / kChunk;
@@ -180,6 +195,8 @@ g4_status launch_sample(g4_ctx* ctx, const uint16_t* logits, int n, float temper
   for (int i = 0; i < n_banned; ++i) sa.banned[i] = banned[i];
   sa.temperature = temperature;
   sa.top_p = top_p;
+  sa.draw_pos = draw_pos;
+  sa.seed = seed;
   const void* fn = (const void*)sample_kernel;
   g4_status st = allow_max_dynamic_smem(ctx, fn, kMaxCand * 8, "sampling");
   if (st != G4_OK) return st;

@@ -22,6 +22,7 @@ LIB.g4_model_last_error.argtypes = [_vp]
 LIB.g4_model_last_error.restype = ctypes.c_char_p
 LIB.g4_model_layer_is_full.argtypes = [_i32]
 LIB.g4_workspace_create.argtypes = [_vp, _vp, _i32, ctypes.POINTER(_vp)]
+LIB.g4_workspace_set_sampling.argtypes = [_vp, ctypes.c_float, _i32, ctypes.c_float, _vp, _i32, _u64]
 LIB.g4_workspace_destroy.argtypes = [_vp]
 LIB.g4_workspace_kv_cache.argtypes = [_vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_u64)]
 LIB.g4_workspace_logits.argtypes = [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_i32)]
@@ -138,6 +139,17 @@ class Workspace:
         dev = f"cuda:{self.ctx.device}"
         torch.cuda.synchronize(dev)
         return (_copy_out(k, n, dev).view(torch.bfloat16), _copy_out(v, n, dev).view(torch.bfloat16))
+
+    def set_sampling(self, temperature: float = 1.0, top_k: int = 0, top_p: float = 1.0, banned=(),
+                     seed: int = 0) -> None:
+        """Sampling mode of the following steps (g4_workspace_set_sampling): top_k 0 is
+        greedy; otherwise top-k / top-p with the device's per-position draw from `seed`."""
+        ids = list(banned)
+        arr = (ctypes.c_int32 * max(1, len(ids)))(*ids)
+        code = LIB.g4_workspace_set_sampling(self.handle, float(temperature), int(top_k), float(top_p),
+                                             ctypes.cast(arr, _vp), len(ids), int(seed) & (2 ** 64 - 1))
+        if code != 0:
+            raise G4Error("g4_workspace_set_sampling", code, "bad sampling parameters")
 
     def logits(self):
         import torch

@@ -383,6 +383,14 @@ int g4_model_layer_is_full(int layer);
  * the context's tensor-parallel world. */
 typedef struct g4_workspace g4_workspace;
 g4_status g4_workspace_create(g4_ctx* ctx, const g4_model* model, int max_positions, g4_workspace** out);
+/* Sampling mode of the decode steps (src/host/generate.rs:214-297 with
+ * src/host/sampling.rs): top_k == 0 is greedy (the default); otherwise every step
+ * draws its token by g4_sample_top_k_top_p's rule with the draw u derived on the device
+ * from (seed, position) (splitmix64 of seed + pos * 0x9E3779B97F4A7C15, top 24 bits / 2^24),
+ * so a run is reproducible and every TP rank draws the same token.  Predictions logged by
+ * g4_decode_predictions are the drawn tokens.  Takes effect at the next step. */
+g4_status g4_workspace_set_sampling(g4_workspace* ws, float temperature, int top_k, float top_p,
+                                    const int32_t* banned, int n_banned, uint64_t seed);
 g4_status g4_workspace_destroy(g4_workspace* ws);
 /* Device pointers of layer `layer`'s K and V caches and their size in bytes each. */
 g4_status g4_workspace_kv_cache(g4_workspace* ws, int layer, g4_bf16** k, g4_bf16** v, uint64_t* bytes);

@@ -85,3 +85,14 @@ def boundary_gap(bits: np.ndarray, temperature: float, top_k: int, top_p: float,
     nucleus = int(np.searchsorted(c, top_p - 1e-7) + 1)
     c = c[:nucleus] / c[nucleus - 1]
     return float(np.min(np.abs(c - u)))
+
+
+def runtime_draw(seed: int, pos: int) -> float:
+    """The decode runtime's draw for the step at `pos` (g4_workspace_set_sampling):
+    splitmix64 of seed + pos * 0x9E3779B97F4A7C15, top 24 bits / 2^24."""
+    m = (1 << 64) - 1
+    z = (seed + (pos & 0xFFFFFFFF) * 0x9E3779B97F4A7C15) & m
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & m
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & m
+    z ^= z >> 31
+    return float(np.float32(z >> 40) * np.float32(1.0 / 16777216.0))

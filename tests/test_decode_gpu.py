@@ -161,6 +161,39 @@ def test_decode_run_is_one_step_of_the_loop(golden):
     assert ctx.poll() == 0
 
 
+def test_sampled_steps_match_oracle_sampler(golden):
+    """Top-k / top-p decode steps (g4_workspace_set_sampling): every step's drawn token is
+    the reference sampler's (oracle/sampling.py) on that step's logits with the runtime's
+    draw for that position, up to draws at a running-sum boundary."""
+    from oracle import sampling as smp
+
+    spec, rm, ctx, ws = _case(golden, "six_layers_long")
+    prompt = golden["six_layers_long.prompt"].tolist()[:24]
+    seed, conf = 1234, (1.0, 64, 0.95, [3, 5])
+    ws.set_sampling(conf[0], conf[1], conf[2], conf[3], seed)
+    try:
+        ws.begin(prompt, 0, 8)
+        same = 0
+        for j in range(len(prompt) + 6):
+            ws.steps(1)
+            bits = ws.logits().cpu().view(torch.int16).numpy().view(np.uint16).copy()
+            got = ws.predictions(j + 1)[-1]
+            u = smp.runtime_draw(seed, j)
+            want = smp.sample(bits, conf[0], conf[1], conf[2], conf[3], u)
+            if got == want:
+                same += 1
+            else:
+                assert smp.boundary_gap(bits, conf[0], conf[1], conf[2], conf[3], u) < 1e-5, (j, got, want)
+        print(f"sampled steps identical to the oracle sampler: {same}/{len(prompt) + 6}")
+        # reproducible: the same seed draws the same tokens
+        a = ws.generate(prompt, 6)
+        b = ws.generate(prompt, 6)
+        assert a == b
+    finally:
+        ws.set_sampling()  # back to greedy for the other tests
+    assert ctx.poll() == 0
+
+
 def test_invalid_position_is_rejected(golden):
     spec, rm, ctx, ws = _case(golden, "six_layers_long")
     with pytest.raises(g4.G4Error):
