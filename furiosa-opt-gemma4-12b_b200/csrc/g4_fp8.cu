@@ -527,9 +527,10 @@ g4_status launch_qkv_fp8(g4_ctx* ctx, bool full, const uint16_t* x, const uint8_
   a.K = H;
   a.in_w = in_w;
   a.D = full ? DF : DS;
-  a.nq = full ? GF : NS * GS;
-  a.nk = full ? 1 : NS;
-  a.nv = full ? 0 : NS;
+  const int tp = ctx->tp_world;  // tensor parallel: this rank's heads (the full layers' K head is replicated)
+  a.nq = (full ? GF : NS * GS) / tp;
+  a.nk = full ? 1 : NS / tp;
+  a.nv = full ? 0 : NS / tp;
   a.nmat = full ? 2 : 3;
   const int rows[3] = {a.nq * a.D, a.nk * a.D, a.nv * a.D};
   for (int i = 0; i < a.nmat; ++i) a.m[i] = fp8::Mat{w[i], rs[i], rows[i]};
@@ -546,7 +547,7 @@ g4_status launch_qkv_fp8(g4_ctx* ctx, bool full, const uint16_t* x, const uint8_
   a.kc = kcache;
   a.vc = vcache;
   a.cache_elems = cache_elems > 0 ? cache_elems
-                                  : (full ? static_cast<long long>(TF) * DF : static_cast<long long>(TS) * NS * DS);
+                                  : (full ? static_cast<long long>(TF) * DF : static_cast<long long>(TS) * a.nk * DS);
   a.q_out = q_out;
   return launch_fp8(ctx, a);
 }

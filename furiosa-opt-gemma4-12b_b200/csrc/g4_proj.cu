@@ -461,11 +461,12 @@ g4_status launch_qkv_fp8(g4_ctx*, bool, const uint16_t*, const uint8_t* const[3]
 g4_status launch_oproj_fp8(g4_ctx*, bool, const uint16_t*, const float*, const uint16_t*, const uint8_t*,
                            const uint16_t*, uint16_t*);
 
-// FP8 projections on one GPU: project_qkv runs on the tensor-core GEMV of g4_fp8.cu, the
-// attention output on the streaming engine (its 240 or 480 row tiles spread over 148 SMs
-// more evenly there: 9 / 11 us against 12.5 / 20.7 us).  G4B200_PROJ_KERNEL=stream or
-// =tensor puts both on one kernel.  NVFP4 weights and tensor-parallel contexts always use
-// the streaming engine.
+// FP8 projections: project_qkv runs on the tensor-core GEMV of g4_fp8.cu (any tensor-
+// parallel size: a rank's heads need no exchange), the attention output on the streaming
+// engine (its 240 or 480 row tiles spread over 148 SMs more evenly there: 9 / 11 us
+// against 12.5 / 20.7 us; under tensor parallelism its in-kernel all-reduce is needed).
+// G4B200_PROJ_KERNEL=stream or =tensor puts both on one kernel (on one GPU).  NVFP4
+// weights always use the streaming engine.
 static int proj_kernel_env() {
   static const int kind = [] {
     const char* e = std::getenv("G4B200_PROJ_KERNEL");
@@ -476,9 +477,9 @@ static int proj_kernel_env() {
   return kind;
 }
 static bool fp8_tensor_path(const g4_ctx* ctx, bool oproj) {
-  if (ctx->tp_world != 1) return false;
   const int kind = proj_kernel_env();
-  return kind == 2 || (kind == 0 && !oproj);
+  if (oproj) return ctx->tp_world == 1 && kind == 2;
+  return kind != 1;
 }
 
 g4_status launch_qkv(g4_ctx* ctx, bool full, bool nvfp4, const uint16_t* x, const uint8_t* const w[3],
