@@ -276,6 +276,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             decode = run_decode(args, ctx, stream, rank, world, dev)
         except Exception as e:  # the headline MLP line still prints
             decode = {"error": f"{type(e).__name__}: {e}"}
+    ops_lines = None
+    if world == 1 and not args.no_ops:
+        try:
+            ops_lines = run_ops(list(OP_BYTES), ctx, stream, dev)
+        except Exception as e:  # the headline MLP line still prints
+            ops_lines = [{"error": f"{type(e).__name__}: {e}"}]
     prefill = None
     if not args.no_prefill:
         try:
@@ -324,9 +330,136 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         line["decode"] = decode
     if prefill is not None:
         line["prefill"] = prefill
+    if ops_lines is not None:
+        line["ops"] = ops_lines
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args)
     return line
+
+
+# Per-op lines (one GPU): the attention-side ops of the decode step and BASELINE configs 2
+# and 3, each cycled over enough distinct weight or cache copies to exceed L2.
+OP_BYTES = {
+    "sliding_qkv": 31473664, "full_qkv": 33440768, "sliding_qkv_nvfp4": 17694720,
+    "sliding_oproj": 15736320, "full_oproj": 31464960,
+    "sliding_attn": 8388608, "full_attn_8192": 8192 * 512 * 2 * 2,
+}
+
+
+def run_ops(names, ctx, stream, dev: str) -> list[dict]:
+    """Times each op through its public wrapper: a CUDA graph of one round over `copies`
+    distinct inputs (> 2x L2 of weights or caches) replayed, CUDA events on the stream."""
+    import torch
+
+    import g4b200 as g4
+
+    g = torch.Generator(device=dev).manual_seed(2)
+
+    def bf(n, std=1.0):
+        return (torch.randn(n, device=dev, generator=g) * std).to(torch.bfloat16)
+
+    def f8(n):  # finite E4M3 codes
+        return torch.randint(0, 256, (n,), dtype=torch.uint8, device=dev, generator=g) & 0x77
+
+    def ones_bf(n):
+        return torch.ones(n, dtype=torch.bfloat16, device=dev)
+
+    pos = 517
+    i32 = lambda v: torch.tensor([v], dtype=torch.int32, device=dev)  # noqa: E731
+    cos_s, sin_s = bf(32768 * 256, 0.5), bf(32768 * 256, 0.5)
+    cos_f, sin_f = bf(32768 * 512, 0.5), bf(32768 * 512, 0.5)
+    peak, peak_kind = measured_peaks()
+    out = []
+    for name in names:
+        nbytes = OP_BYTES[name]
+        copies = max(2, -(-320_000_000 // nbytes))
+        calls = []
+        if name in ("sliding_qkv", "full_qkv", "sliding_qkv_nvfp4"):
+            full = name == "full_qkv"
+            D = 512 if full else 256
+            rows = (8192, 512, 0) if full else (4096, 2048, 2048)
+            x, in_w, qn, kn = bf(H), ones_bf(H), ones_bf(D), ones_bf(D)
+            kv_off = i32((pos % 512) * 512 * 2 if full else (pos % 1024) * 8 * 256 * 2)
+            rope_off = i32(pos * D * 2)
+            kc = torch.zeros((512 if full else 1024 * 8) * D, dtype=torch.bfloat16, device=dev)
+            vc = torch.zeros_like(kc)
+            q_out = torch.zeros(rows[0], dtype=torch.bfloat16, device=dev)
+            cs, sn = (cos_f, sin_f) if full else (cos_s, sin_s)
+            for _ in range(copies):
+                if name == "sliding_qkv_nvfp4":
+                    w = [f8(r * H // 2) for r in rows]
+                    bs = [(torch.randint(0x30, 0x40, (r * H // 16,), dtype=torch.uint8, device=dev, generator=g))
+                          for r in rows]
+                    gs = [torch.full((1,), 1.0 / 64, dtype=torch.float32, device=dev) for _ in rows]
+                    a = (x, *w, *bs, *gs, in_w, qn, kn, kv_off, rope_off, cs, sn, kc, vc, q_out)
+                    calls.append(lambda a=a: g4.sliding_project_qkv_nvfp4(ctx, *a))
+                elif full:
+                    a = (x, f8(rows[0] * H), f8(rows[1] * H), bf(rows[0], 0.01), bf(rows[1], 0.01), in_w, qn, kn,
+                         kv_off, rope_off, cs, sn, kc, vc, q_out)
+                    calls.append(lambda a=a: g4.full_project_qkv(ctx, *a))
+                else:
+                    a = (x, f8(rows[0] * H), f8(rows[1] * H), f8(rows[2] * H), bf(rows[0], 0.01), bf(rows[1], 0.01),
+                         bf(rows[2], 0.01), in_w, qn, kn, kv_off, rope_off, cs, sn, kc, vc, q_out)
+                    calls.append(lambda a=a: g4.sliding_project_qkv(ctx, *a))
+        elif name in ("sliding_oproj", "full_oproj"):
+            full = name == "full_oproj"
+            K = 8192 if full else 4096
+            x, pw, res = bf(K), ones_bf(H), bf(H)
+            rsum = torch.ones(16, dtype=torch.float32, device=dev)
+            for _ in range(copies):
+                w, sc = f8(H * K), bf(H, 0.001)
+                if full:
+                    calls.append(lambda w=w, sc=sc: g4.full_attention_output(ctx, x, rsum, pw, w, sc, res))
+                else:
+                    calls.append(lambda w=w, sc=sc: g4.sliding_attention_output(ctx, x, pw, w, sc, res))
+        elif name == "sliding_attn":
+            q, mask, o = bf(4096), torch.ones(1024, dtype=torch.float32, device=dev), bf(4096)
+            for _ in range(copies):
+                k, v = bf(1024 * 8 * 256), bf(1024 * 8 * 256)
+                calls.append(lambda k=k, v=v: g4.sliding_attention(ctx, q, k, v, mask, o))
+        else:  # full_attn_8192: the reference's page cache, 16 pages of [512, 512]
+            q, o = bf(16 * 512), bf(16 * 512)
+            rsum = torch.ones(16, dtype=torch.float32, device=dev)
+            for _ in range(copies):
+                kp, vp = bf(16 * 512 * 512), bf(16 * 512 * 512)
+                ka = torch.tensor([kp.data_ptr() + i * 512 * 512 * 2 for i in range(16)], dtype=torch.int64,
+                                  device=dev)
+                va = torch.tensor([vp.data_ptr() + i * 512 * 512 * 2 for i in range(16)], dtype=torch.int64,
+                                  device=dev)
+                calls.append(lambda ka=ka, va=va, kp=kp, vp=vp: g4.full_attention_paged(ctx, q, ka, va, 16, 511,
+                                                                                       rsum, o))
+        with torch.cuda.stream(stream):
+            for c in calls:
+                c()
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for c in calls:
+                c()
+        reps = max(3, 4000 // len(calls))
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                graph.replay()
+            stream.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            e1.record(stream)
+            stream.synchronize()
+        us = e0.elapsed_time(e1) * 1000.0 / (reps * len(calls))
+        del graph, calls
+        achieved = nbytes / (us * 1e-6) / 1e9
+        out.append({"op": name, "value": round(us, 3), "unit": "µs/call", "copies": copies,
+                    "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                                 "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                                 "algorithmic_bytes_per_call": nbytes},
+                    "launch": "CUDA graph of one round over the copies, replayed; consecutive calls overlap via "
+                              "programmatic dependent launch"})
+    status = ctx.poll()
+    for o in out:
+        o["device_status"] = status
+    return out
 
 
 def run_only(args, rank: int, world: int, local_rank: int) -> dict | None:
@@ -347,7 +480,13 @@ def run_only(args, rank: int, world: int, local_rank: int) -> dict | None:
         tpinfo = (rank, world, nid[0])
     ctx = g4.Context(local_rank, stream=stream, tp=tpinfo)
     try:
-        out = (run_decode if args.only == "decode" else run_prefill)(args, ctx, stream, rank, world, dev)
+        if args.only == "ops":
+            if world > 1:
+                return None
+            names = list(OP_BYTES) if args.op == "all" else [args.op]
+            out = {"ops": run_ops(names, ctx, stream, dev)}
+        else:
+            out = (run_decode if args.only == "decode" else run_prefill)(args, ctx, stream, rank, world, dev)
     finally:
         ctx.close()
     return out if rank == 0 else None
@@ -612,8 +751,10 @@ def main() -> None:
     ap.add_argument("--no-prefill", action="store_true", help="skip the batched prefill MLP measurement")
     ap.add_argument("--prefill-tokens", type=int, default=4096)
     ap.add_argument("--prefill-reps", type=int, default=30)
-    ap.add_argument("--only", choices=["decode", "prefill"], default=None,
-                    help="run just the whole-model decode or the prefill measurement (e.g. under a profiler)")
+    ap.add_argument("--only", choices=["decode", "prefill", "ops"], default=None,
+                    help="run just the whole-model decode, the prefill or the per-op measurement")
+    ap.add_argument("--op", choices=["all", *OP_BYTES], default="all", help="with --only ops: which op")
+    ap.add_argument("--no-ops", action="store_true", help="skip the per-op lines")
     ap.add_argument("--mlp-kernel", choices=["auto", "stream", "tensor"], default="auto",
                     help="decoder_feedforward kernel: streaming (CUDA-core decode) or tcgen05 (one GPU)")
     args = ap.parse_args()
