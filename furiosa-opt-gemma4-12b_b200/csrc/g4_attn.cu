@@ -623,13 +623,17 @@ __global__ void __launch_bounds__(kFaMergeThreads) fa_merge_kernel(const float* 
 // Same math as sliding_attn_kernel with 128-slot chunks.
 constexpr int kScRows = 128;
 constexpr int kScCtas = TS / kScRows;  // 8: the cluster
-constexpr int kScThreads = 256;
+constexpr int kScThreads = 512;
+constexpr int kScWarps = kScThreads / 32;
+constexpr int kScRpw = kScRows / kScWarps;  // slots per warp: 8
+static_assert(GS * kScRpw == 16, "the scores' butterfly sums 16 values per lane");
+static_assert(GS * DS == kScThreads, "one output per thread in the cross-warp sum");
 constexpr int kScBox = kScRows / 16;   // slots per TMA box
 
 struct __align__(128) ScSmem {  // TMA destinations: 128-byte aligned
   uint16_t k[kScRows][DS];
   uint16_t v[kScRows][DS];
-  float red[kScThreads / 32][GS][DS];
+  float red[kScWarps][GS][DS];
   float q[GS][DS];
   float o[GS][DS];  // this CTA's partial weighted sums (read by the cluster)
   float s[GS][kScRows];
@@ -698,30 +702,45 @@ __global__ void __launch_bounds__(kScThreads) sliding_attn_cluster_kernel(const 
   __syncthreads();
   if (!mbar_wait(&sm.full, 0u, deadline)) atomicOr(&scr->status, DEV_ERR_TIMEOUT_MBAR);
   pdl_launch_dependents();
-  // scores: warp w owns slots 16 w .. 16 w + 15, lane l dims 8 l .. 8 l + 7
-  float qa[8], qb[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    qa[i] = sm.q[0][8 * lane + i];
-    qb[i] = sm.q[1][8 * lane + i];
-  }
-#pragma unroll 4
-  for (int j = 0; j < 16; ++j) {
-    const int row = 16 * warp + j;
-    float kf[8];
-    bf16x8_to_f32(*reinterpret_cast<const uint4*>(&sm.k[row][8 * lane]), kf);
-    float d0 = 0.f, d1 = 0.f;
+  // scores: warp w owns slots 8 w .. 8 w + 7, lane l dims 8 l .. 8 l + 7; a lane's 16
+  // partial dot products (2 q heads x 8 slots) are summed over the warp by a butterfly
+  // that halves the values held per step (16 shuffles instead of 16 x 5): lane l ends
+  // with the sum of value l % 16 (q head (l % 16) / 8, slot 8 w + l % 8)
+  {
+    float qa[8], qb[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      d0 = fmaf(qa[i], kf[i], d0);
-      d1 = fmaf(qb[i], kf[i], d1);
+      qa[i] = sm.q[0][8 * lane + i];
+      qb[i] = sm.q[1][8 * lane + i];
     }
-    d0 = warp_sum(d0);
-    d1 = warp_sum(d1);
-    if (lane == 0) {
-      const bool ok = sm.valid[row] > 0.f;
-      sm.s[0][row] = ok ? d0 : -CUDART_INF_F;
-      sm.s[1][row] = ok ? d1 : -CUDART_INF_F;
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < kScRpw; ++j) {
+      float kf[8];
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(&sm.k[kScRpw * warp + j][8 * lane]), kf);
+      float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        d0 = fmaf(qa[i], kf[i], d0);
+        d1 = fmaf(qb[i], kf[i], d1);
+      }
+      v[j] = d0;
+      v[8 + j] = d1;
+    }
+#pragma unroll
+    for (int off = 8; off >= 1; off >>= 1) {
+      const bool up = (lane & off) != 0;
+#pragma unroll
+      for (int k = 0; k < off; ++k) {
+        const float send = up ? v[k] : v[k + off];
+        const float keep = up ? v[k + off] : v[k];
+        v[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+      }
+    }
+    v[0] += __shfl_xor_sync(0xffffffffu, v[0], 16);
+    if (lane < 16) {
+      const int hh = lane >> 3, row = kScRpw * warp + (lane & 7);
+      sm.s[hh][row] = sm.valid[row] > 0.f ? v[0] : -CUDART_INF_F;
     }
   }
   __syncthreads();
@@ -746,33 +765,39 @@ __global__ void __launch_bounds__(kScThreads) sliding_attn_cluster_kernel(const 
     }
   }
   __syncthreads();
-  float o0[8], o1[8];
+  // weighted V sum: warp w its 8 slots, lane l dims 8 l .. 8 l + 7, then the 16 warps'
+  // sums added in warp order
+  {
+    float o0[8], o1[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) o0[i] = o1[i] = 0.f;
-#pragma unroll 4
-  for (int j = 0; j < 16; ++j) {
-    const int row = 16 * warp + j;
-    if (sm.valid[row] > 0.f) {  // unused ring slots may hold anything: never touched
-      float vf[8];
-      bf16x8_to_f32(*reinterpret_cast<const uint4*>(&sm.v[row][8 * lane]), vf);
-      const float p0 = sm.s[0][row], p1 = sm.s[1][row];
+    for (int i = 0; i < 8; ++i) o0[i] = o1[i] = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        o0[i] = fmaf(p0, vf[i], o0[i]);
-        o1[i] = fmaf(p1, vf[i], o1[i]);
+    for (int j = 0; j < kScRpw; ++j) {
+      const int row = kScRpw * warp + j;
+      if (sm.valid[row] > 0.f) {  // unused ring slots may hold anything: never touched
+        float vf[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(&sm.v[row][8 * lane]), vf);
+        const float p0 = sm.s[0][row], p1 = sm.s[1][row];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          o0[i] = fmaf(p0, vf[i], o0[i]);
+          o1[i] = fmaf(p1, vf[i], o1[i]);
+        }
       }
     }
-  }
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    sm.red[warp][0][8 * lane + i] = o0[i];
-    sm.red[warp][1][8 * lane + i] = o1[i];
+    float4* r0 = reinterpret_cast<float4*>(&sm.red[warp][0][8 * lane]);
+    float4* r1 = reinterpret_cast<float4*>(&sm.red[warp][1][8 * lane]);
+    r0[0] = make_float4(o0[0], o0[1], o0[2], o0[3]);
+    r0[1] = make_float4(o0[4], o0[5], o0[6], o0[7]);
+    r1[0] = make_float4(o1[0], o1[1], o1[2], o1[3]);
+    r1[1] = make_float4(o1[4], o1[5], o1[6], o1[7]);
   }
   __syncthreads();
-  for (int o = tid; o < GS * DS; o += kScThreads) {
+  {
+    const int o = tid;  // GS * DS == kScThreads outputs, one per thread
     float acc = 0.f;
 #pragma unroll
-    for (int w = 0; w < kScThreads / 32; ++w) acc += sm.red[w][o / DS][o % DS];
+    for (int w = 0; w < kScWarps; ++w) acc += sm.red[w][o / DS][o % DS];
     sm.o[o / DS][o % DS] = acc;
   }
   cluster_sync_all();  // every CTA's partial is complete and visible to the cluster
