@@ -391,8 +391,8 @@ constexpr int kFaPart = 2 * GF + GF * DF;        // m[16], l[16], o[16][512]
 constexpr int kFaMaxCtas = 512;
 
 struct FaSmem {
-  uint8_t k[kFaTile * DF * 2];
-  uint8_t v[kFaTile * DF * 2];
+  uint8_t k[2][kFaTile * DF * 2];  // two tiles: the next one loads while this one computes
+  uint8_t v[2][kFaTile * DF * 2];
   uint8_t q[GF * kFaQStride];
   float s[GF][kFaTile + 1];
   float m[GF], l[GF], alpha[GF];
@@ -441,12 +441,27 @@ __global__ void __launch_bounds__(kFaThreads) fa_partial_kernel(const uint16_t* 
     pdl_launch_dependents();
     return;
   }
-  const uint32_t qb = smem_u32(sm.q), kb = smem_u32(sm.k), vb = smem_u32(sm.v);
+  const uint32_t qb = smem_u32(sm.q);
   for (int i = tid; i < GF * (DF / 8); i += kFaThreads) {
     const int hh = i / (DF / 8), c = i % (DF / 8);
     const bool ok = hh < nq;
     cp_async16(qb + hh * kFaQStride + c * 16, ok ? q + hh * DF + c * 8 : q, ok ? 16u : 0u);
   }
+  // tile loads: rows [tr, tr + 32) into buffer b, one cp.async group per tile
+  auto load_tile = [&](int tr, int b) {
+    const uint32_t kbb = smem_u32(sm.k[b]), vbb = smem_u32(sm.v[b]);
+    for (int i = tid; i < kFaTile * (DF / 8); i += kFaThreads) {
+      const int rr = i / (DF / 8), c = i % (DF / 8);
+      const int r = tr + rr;
+      const bool ok = r < r1;
+      const uint32_t off = rr * (DF * 2) + ((c ^ (rr & 7)) * 16);
+      cp_async16(kbb + off, ok ? fa_row(src, false, r) + c * 8 : q, ok ? 16u : 0u);
+      cp_async16(vbb + off, ok ? fa_row(src, true, r) + c * 8 : q, ok ? 16u : 0u);
+    }
+    cp_async_commit();
+  };
+  load_tile(r0, 0);
+  if (r0 + kFaTile < r1) load_tile(r0 + kFaTile, 1);
   if (tid < GF) {
     sm.m[tid] = -CUDART_INF_F;
     sm.l[tid] = 0.f;
@@ -455,17 +470,13 @@ __global__ void __launch_bounds__(kFaThreads) fa_partial_kernel(const uint16_t* 
 #pragma unroll
   for (int nt = 0; nt < 16; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
 
-  for (int tr = r0; tr < r1; tr += kFaTile) {
-    for (int i = tid; i < kFaTile * (DF / 8); i += kFaThreads) {
-      const int rr = i / (DF / 8), c = i % (DF / 8);
-      const int r = tr + rr;
-      const bool ok = r < r1;
-      const uint32_t off = rr * (DF * 2) + ((c ^ (rr & 7)) * 16);
-      cp_async16(kb + off, ok ? fa_row(src, false, r) + c * 8 : q, ok ? 16u : 0u);
-      cp_async16(vb + off, ok ? fa_row(src, true, r) + c * 8 : q, ok ? 16u : 0u);
-    }
-    if (tr == r0) pdl_launch_dependents();
-    cp_async_wait_all();
+  pdl_launch_dependents();
+  for (int tr = r0, ti = 0; tr < r1; tr += kFaTile, ++ti) {
+    const uint32_t kb = smem_u32(sm.k[ti & 1]), vb = smem_u32(sm.v[ti & 1]);
+    if (tr + kFaTile < r1)
+      cp_async_wait_group<1>();  // this tile (and q) landed; the next may still fly
+    else
+      cp_async_wait_group<0>();
     __syncthreads();
     // S[16 heads][8 rows of this warp] = Q K^T over the 512 dims
     float sc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -543,7 +554,8 @@ __global__ void __launch_bounds__(kFaThreads) fa_partial_kernel(const uint16_t* 
         mma_bf16(acc[nt + 1], lo[0], lo[1], lo[2], lo[3], b2, b3);
       }
     }
-    __syncthreads();  // the next tile overwrites K, V and S
+    __syncthreads();  // buffer ti & 1 and S are free again
+    if (tr + 2 * kFaTile < r1) load_tile(tr + 2 * kFaTile, ti & 1);
   }
   float* mine = part + static_cast<size_t>(blockIdx.x) * kFaPart;
   if (tid < GF) {
@@ -559,13 +571,16 @@ __global__ void __launch_bounds__(kFaThreads) fa_partial_kernel(const uint16_t* 
 }
 
 // Four CTAs per head, 128 dims each: the active partials' (m, l) in one parallel load,
-// their weights once, then each output's partial values with independent loads, added in
-// CTA order.
-constexpr int kFaMergeThreads = 128;
+// their weights once; then four thread groups each add a quarter of the partials of every
+// output (independent loads, eight in flight per thread) and the groups' sums are added in
+// group order.
+constexpr int kFaMergeThreads = 512;
+constexpr int kFaMergeGroups = kFaMergeThreads / 128;
 __global__ void __launch_bounds__(kFaMergeThreads) fa_merge_kernel(const float* part, FaSrc src, int grid,
                                                                    float* running_sum, uint16_t* out) {
   __shared__ float w[kFaMaxCtas];
   __shared__ float red[kFaMergeThreads / 32];
+  __shared__ float osum[kFaMergeGroups][128];
   __shared__ float Mall, Lall;
   const int h = blockIdx.x >> 2, quarter = blockIdx.x & 3, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   pdl_wait();  // every partial of the previous kernel is written
@@ -604,13 +619,21 @@ __global__ void __launch_bounds__(kFaMergeThreads) fa_merge_kernel(const float* 
     Lall = x;
   }
   __syncthreads();
-  const int d = quarter * kFaMergeThreads + tid;
+  const int dl = tid & 127, grp = tid >> 7;
+  const int d = quarter * 128 + dl;
   const float* src_o = part + 2 * GF + h * DF + d;
   float o = 0.f;
 #pragma unroll 8
-  for (int p = 0; p < nact; ++p) o += w[p] * __ldcg(src_o + static_cast<size_t>(p) * kFaPart);
-  out[h * DF + d] = f32_to_bf16(Lall > 0.f ? o / Lall : 0.f);
-  if (quarter == 0 && tid == 0) running_sum[h] = 1.0f;
+  for (int p = grp; p < nact; p += kFaMergeGroups) o += w[p] * __ldcg(src_o + static_cast<size_t>(p) * kFaPart);
+  osum[grp][dl] = o;
+  __syncthreads();
+  if (grp == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int gi = 0; gi < kFaMergeGroups; ++gi) t += osum[gi][dl];
+    out[h * DF + d] = f32_to_bf16(Lall > 0.f ? t / Lall : 0.f);
+    if (quarter == 0 && tid == 0) running_sum[h] = 1.0f;
+  }
 }
 
 // ---------------------------------------------------------------------------- sliding, clustered
