@@ -641,9 +641,14 @@ __global__ void __launch_bounds__(kFaMergeThreads) fa_merge_kernel(const float* 
 // [128 r, 128 r + 128) of K and V into shared memory as 16 TMA boxes each (the cache
 // viewed as [slot][kv head][256]: box 8 slots x 1 head x 256), computes its partial
 // softmax statistics and weighted V sum for the head's 2 q heads, and the cluster merges
-// the 8 partials through distributed shared memory (CTA r finishes dims [32 r, 32 r + 32)
-// of both heads, adding the partials in CTA order) -- no global round trip, no counter.
-// Same math as sliding_attn_kernel with 128-slot chunks.
+// the 8 partials through distributed shared memory: CTA r stores dims [32 c, 32 c + 32)
+// of its partial into CTA c's shared memory, one cluster barrier, and CTA c adds the 8
+// partials of its dims in CTA order -- no global round trip, no counter.
+// The copies start before griddepcontrol.wait.  A ring slot is rewritten only by the
+// attention projection of the same layer: when the launch knows that projection's
+// device offset (`fresh`, its kv_off), the CTA holding that slot copies its K and V rows
+// again after the wait; every other slot was written by kernels that completed before
+// this launch could start.  Same math as sliding_attn_kernel with 128-slot chunks.
 constexpr int kScRows = 128;
 constexpr int kScCtas = TS / kScRows;  // 8: the cluster
 constexpr int kScThreads = 512;
@@ -658,7 +663,8 @@ struct __align__(128) ScSmem {  // TMA destinations: 128-byte aligned
   uint16_t v[kScRows][DS];
   float red[kScWarps][GS][DS];
   float q[GS][DS];
-  float o[GS][DS];  // this CTA's partial weighted sums (read by the cluster)
+  float mo[kScCtas][GS][32];  // partial weighted sums of this CTA's 32 dims, from CTA c
+  float mm[kScCtas][GS], ml[kScCtas][GS];  // and CTA c's softmax max / sum
   float s[GS][kScRows];
   float valid[kScRows];
   float m[GS], l[GS];
@@ -670,15 +676,21 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
-__device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t rank) {
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Store to the same shared-memory variable in CTA `rank` of the cluster.
+__device__ __forceinline__ void st_cluster_f32(float* local, uint32_t rank, float v) {
   uint32_t remote;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-  return v;
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
 }
 
 __device__ __forceinline__ void tma_3d_load(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar,
@@ -694,7 +706,8 @@ __global__ void __launch_bounds__(kScThreads) sliding_attn_cluster_kernel(const 
                                                                           const __grid_constant__ CUtensorMap vmap,
                                                                           const uint16_t* q, const float* mask,
                                                                           uint16_t* out, Scratch* scr,
-                                                                          uint64_t budget_ns) {
+                                                                          uint64_t budget_ns, const uint16_t* kc,
+                                                                          const uint16_t* vc, const int32_t* fresh) {
   extern __shared__ uint8_t sc_raw[];
   ScSmem& sm = *reinterpret_cast<ScSmem*>((reinterpret_cast<uintptr_t>(sc_raw) + 127) & ~uintptr_t(127));
   const uint32_t r = cluster_ctarank();
@@ -706,8 +719,7 @@ __global__ void __launch_bounds__(kScThreads) sliding_attn_cluster_kernel(const 
     fence_mbar_init();
   }
   __syncthreads();
-  pdl_wait();  // q, the caches and the mask come from earlier kernels
-  const uint64_t deadline = global_ns() + budget_ns;
+  cluster_arrive_relaxed();  // waited for before the first store into another CTA
   if (warp == 0) {
     // 16 boxes of 8 slots per tensor, one per lane: many copies in flight at once
     const uint64_t pol = l2_evict_first_policy();  // 335 MB of rings per token: streamed
@@ -719,11 +731,25 @@ __global__ void __launch_bounds__(kScThreads) sliding_attn_cluster_kernel(const 
     else
       tma_3d_load(sm.v[kScBox * b], &vmap, 0, h, row0 + kScBox * b, &sm.full, pol);
   }
+  pdl_wait();  // q, the mask and the newest cache row come from earlier kernels
+  const uint64_t deadline = global_ns() + budget_ns;
   for (int i = tid; i < GS * DS; i += kScThreads)
     sm.q[i / DS][i % DS] = bf16_to_f32(q[static_cast<size_t>(h) * GS * DS + i]);
   if (tid < kScRows) sm.valid[tid] = mask[row0 + tid];
-  __syncthreads();
+  const int nkv = static_cast<int>(gridDim.x) / kScCtas;
+  int fslot = -1;  // the slot the projection just wrote, when this CTA holds it
+  if (fresh != nullptr) {
+    const long long off = static_cast<long long>(*fresh) / 2;  // element offset of the slot's row
+    const long long slot = off / (static_cast<long long>(nkv) * DS);
+    if (off >= 0 && slot >= row0 && slot < row0 + kScRows) fslot = static_cast<int>(slot);
+  }
   if (!mbar_wait(&sm.full, 0u, deadline)) atomicOr(&scr->status, DEV_ERR_TIMEOUT_MBAR);
+  if (fslot >= 0 && tid < 64) {  // after the boxes landed: these stores come last
+    const size_t src = (static_cast<size_t>(fslot) * nkv + h) * DS + 8 * (tid & 31);
+    const uint4 w = *reinterpret_cast<const uint4*>((tid < 32 ? kc : vc) + src);
+    *reinterpret_cast<uint4*>(tid < 32 ? &sm.k[fslot - row0][8 * (tid & 31)] : &sm.v[fslot - row0][8 * (tid & 31)]) = w;
+  }
+  __syncthreads();
   pdl_launch_dependents();
   // scores: warp w owns slots 8 w .. 8 w + 7, lane l dims 8 l .. 8 l + 7; a lane's 16
   // partial dot products (2 q heads x 8 slots) are summed over the warp by a butterfly
@@ -816,22 +842,32 @@ __global__ void __launch_bounds__(kScThreads) sliding_attn_cluster_kernel(const 
     r1[1] = make_float4(o1[4], o1[5], o1[6], o1[7]);
   }
   __syncthreads();
+  cluster_wait();  // every CTA of the cluster is running: its shared memory may be written
   {
     const int o = tid;  // GS * DS == kScThreads outputs, one per thread
+    const int hh = o / DS, d = o % DS;
     float acc = 0.f;
 #pragma unroll
-    for (int w = 0; w < kScWarps; ++w) acc += sm.red[w][o / DS][o % DS];
-    sm.o[o / DS][o % DS] = acc;
+    for (int w = 0; w < kScWarps; ++w) acc += sm.red[w][hh][d];
+    st_cluster_f32(&sm.mo[r][hh][d % 32], static_cast<uint32_t>(d / 32), acc);  // to the CTA finishing dim d
+    if (tid < GS * kScCtas) {
+      const int gh = tid / kScCtas, c = tid % kScCtas;
+      st_cluster_f32(&sm.mm[r][gh], static_cast<uint32_t>(c), sm.m[gh]);
+      st_cluster_f32(&sm.ml[r][gh], static_cast<uint32_t>(c), sm.l[gh]);
+    }
   }
-  cluster_sync_all();  // every CTA's partial is complete and visible to the cluster
+  // Every CTA's partials are in place; after this barrier a CTA reads only its own shared
+  // memory, so it may exit as soon as it is done.
+  cluster_arrive_release();
+  cluster_wait_acquire();
   if (tid < GS * 32) {
-    const int hh = tid >> 5, d = 32 * static_cast<int>(r) + (tid & 31);
+    const int hh = tid >> 5, dl = tid & 31, d = 32 * static_cast<int>(r) + dl;
     float mc[kScCtas], lc[kScCtas], oc[kScCtas], mx = -CUDART_INF_F;
 #pragma unroll
     for (int c = 0; c < kScCtas; ++c) {
-      mc[c] = ld_cluster_f32(&sm.m[hh], static_cast<uint32_t>(c));
-      lc[c] = ld_cluster_f32(&sm.l[hh], static_cast<uint32_t>(c));
-      oc[c] = ld_cluster_f32(&sm.o[hh][d], static_cast<uint32_t>(c));
+      mc[c] = sm.mm[c][hh];
+      lc[c] = sm.ml[c][hh];
+      oc[c] = sm.mo[c][hh][dl];
       mx = fmaxf(mx, mc[c]);
     }
     float ls = 0.f, acc = 0.f;
@@ -843,7 +879,6 @@ __global__ void __launch_bounds__(kScThreads) sliding_attn_cluster_kernel(const 
     }
     out[(static_cast<size_t>(h) * GS + hh) * DS + d] = f32_to_bf16(ls > 0.f ? acc / ls : 0.f);
   }
-  cluster_sync_all();  // no CTA leaves while the others read its shared memory
 }
 
 // ---------------------------------------------------------------------------- launchers
@@ -902,6 +937,8 @@ static bool cache_map(CUtensorMap* m, const void* base, int nkv) {
 // where the runtime refuses the cluster launch, the split-KV kernel with a global merge.
 g4_status launch_sliding_attention(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
                                    const float* mask, uint16_t* out) {
+  // the newest row of this cache, when the last projection on this context wrote it
+  const int32_t* fresh = (ctx->qkv_kc == k) ? ctx->qkv_kv_off : nullptr;
   CUtensorMap km, vm;
   const int nkv = NS / ctx->tp_world;
   if (ctx->cluster_ok && cache_map(&km, k, nkv) && cache_map(&vm, v, nkv)) {
@@ -911,7 +948,8 @@ g4_status launch_sliding_attention(g4_ctx* ctx, const uint16_t* q, const uint16_
     if (st != G4_OK) return st;
     Scratch* scr = ctx->buf.scratch;
     uint64_t budget = ctx->wait_budget_ns;
-    void* args[] = {(void*)&km, (void*)&vm, (void*)&q, (void*)&mask, (void*)&out, (void*)&scr, (void*)&budget};
+    void* args[] = {(void*)&km,  (void*)&vm,     (void*)&q, (void*)&mask, (void*)&out,
+                    (void*)&scr, (void*)&budget, (void*)&k, (void*)&v,    (void*)&fresh};
     if (launch_kernel(ctx, fn, dim3(nkv * kScCtas), dim3(kScThreads), smem, args, false, "sliding attention",
                       kScCtas) == G4_OK)
       return G4_OK;

@@ -102,6 +102,11 @@ struct g4_ctx {
   bool coop_ok = true;
   bool pdl_ok = true;  // programmatic dependent launch accepted by the runtime
   bool cluster_ok = true;  // thread-block cluster launches accepted
+  // The K cache and device offset of the last attention projection launched on this
+  // context: sliding attention over that cache re-reads the row it wrote after waiting
+  // for its predecessor (the other rows it copies before).
+  const uint16_t* qkv_kc = nullptr;
+  const int32_t* qkv_kv_off = nullptr;
   int mlp_kernel = 0;  // G4_MLP_AUTO / G4_MLP_STREAM / G4_MLP_TENSOR
   g4::PeerXch peers = {};  // TP exchange buffers mapped from every rank (world 0: NCCL path)
   g4::PrefillBuffers prefill;

@@ -487,6 +487,8 @@ g4_status launch_qkv(g4_ctx* ctx, bool full, bool nvfp4, const uint16_t* x, cons
                      const uint16_t* in_w, const uint16_t* qn_w, const uint16_t* kn_w, const int32_t* kv_off,
                      const int32_t* rope_off, const uint16_t* cosT, const uint16_t* sinT, uint16_t* kcache,
                      uint16_t* vcache, uint16_t* q_out, long long cache_elems) {
+  ctx->qkv_kc = kcache;
+  ctx->qkv_kv_off = kv_off;
   if (!nvfp4 && fp8_tensor_path(ctx, false))
     return launch_qkv_fp8(ctx, full, x, w, rs, in_w, qn_w, kn_w, kv_off, rope_off, cosT, sinT, kcache, vcache, q_out,
                           cache_elems);
