@@ -463,8 +463,9 @@ g4_status launch_oproj_fp8(g4_ctx*, bool, const uint16_t*, const float*, const u
 
 // FP8 projections: project_qkv runs on the tensor-core GEMV of g4_fp8.cu (any tensor-
 // parallel size: a rank's heads need no exchange), the attention output on the streaming
-// engine (its 240 or 480 row tiles spread over 148 SMs more evenly there: 9 / 11 us
-// against 12.5 / 20.7 us; under tensor parallelism its in-kernel all-reduce is needed).
+// engine (9.1 / 11.7 us per sliding / full call against 10.1 / 16.5 us there: its work per
+// CTA is small and the GEMV's fixed costs weigh more; under tensor parallelism the
+// streaming engine's in-kernel all-reduce is needed).
 // G4B200_PROJ_KERNEL=stream or =tensor puts both on one kernel (on one GPU).  NVFP4
 // weights always use the streaming engine.
 static int proj_kernel_env() {
