@@ -270,6 +270,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
     del e2e_graphs
 
+    in_step = None
+    if world == 1 and not args.no_ops:
+        try:
+            in_step = run_mlp_in_step(ctx, stream, layers, residual, dev)
+        except Exception as e:  # the headline MLP line still prints
+            in_step = {"error": f"{type(e).__name__}: {e}"}
     decode = None
     if not args.no_decode:
         try:
@@ -326,6 +332,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "clocks": sampler.summary(),
         "device_status": status,
     }
+    if in_step is not None:
+        line["mlp_in_step"] = in_step
     if decode is not None:
         line["decode"] = decode
     if prefill is not None:
@@ -344,6 +352,74 @@ OP_BYTES = {
     "sliding_oproj": 15736320, "full_oproj": 31464960,
     "sliding_attn": 8388608, "full_attn_8192": 8192 * 512 * 2 * 2,
 }
+
+
+def run_mlp_in_step(ctx, stream, layers, residual, dev: str) -> dict:
+    """The MLP's cost next to another kernel, as in a decode step: a CUDA graph of
+    NLAYERS x (decoder_feedforward, then sliding_project_qkv reading its residual) against
+    one of the NLAYERS projections alone; the difference per layer is what the MLP adds
+    when its prologue overlaps a projection instead of another MLP's tail."""
+    import torch
+
+    import g4b200 as g4
+
+    g = torch.Generator(device=dev).manual_seed(5)
+
+    def bf(n, std=1.0):
+        return (torch.randn(n, device=dev, generator=g) * std).to(torch.bfloat16)
+
+    def f8(n):
+        return torch.randint(0, 256, (n,), dtype=torch.uint8, device=dev, generator=g) & 0x77
+
+    ones = torch.ones(H, dtype=torch.bfloat16, device=dev)
+    qn = torch.ones(256, dtype=torch.bfloat16, device=dev)
+    i32 = lambda v: torch.tensor([v], dtype=torch.int32, device=dev)  # noqa: E731
+    kv_off, rope_off = i32((517 % 1024) * 8 * 256 * 2), i32(517 * 256 * 2)
+    cs, sn = bf(32768 * 256, 0.5), bf(32768 * 256, 0.5)
+    kc = torch.zeros(1024 * 8 * 256, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    q_out = torch.zeros(4096, dtype=torch.bfloat16, device=dev)
+    qkv = [(f8(4096 * H), f8(2048 * H), f8(2048 * H), bf(4096, 0.01), bf(2048, 0.01), bf(2048, 0.01))
+           for _ in range(NLAYERS)]
+
+    def mlp(j):
+        m = dict(layers[j])
+        m["residual"] = residual
+        g4.decoder_feedforward(ctx, **m)
+
+    def proj(j):
+        w = qkv[j]
+        g4.sliding_project_qkv(ctx, residual, w[0], w[1], w[2], w[3], w[4], w[5], ones, qn, qn, kv_off, rope_off,
+                               cs, sn, kc, vc, q_out)
+
+    def timed(fn) -> float:
+        with torch.cuda.stream(stream):
+            for j in range(NLAYERS):
+                fn(j)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for j in range(NLAYERS):
+                fn(j)
+        reps = 500
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                graph.replay()
+            stream.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            e1.record(stream)
+            stream.synchronize()
+        del graph
+        return e0.elapsed_time(e1) * 1000.0 / (reps * NLAYERS)
+
+    pair = timed(lambda j: (mlp(j), proj(j)))
+    alone = timed(proj)
+    return {"value": round(pair - alone, 3), "unit": "µs/token", "pair_us": round(pair, 3),
+            "projection_alone_us": round(alone, 3), "device_status": ctx.poll(),
+            "how": "graph of decoder_feedforward + sliding_project_qkv per layer, minus the projections alone"}
 
 
 def run_ops(names, ctx, stream, dev: str) -> list[dict]:
