@@ -72,10 +72,11 @@ def profile_traffic(kernel: str) -> float | None:
 
 def mlp_kernel_name(choice: str, world: int, peer: bool = False) -> str:
     """Kernel decoder_feedforward runs with this bench choice (the library's own rule:
-    the tcgen05 kernel on one GPU, the streaming kernel under tensor parallelism)."""
+    the tcgen05 kernel on one GPU and on TP2 contexts that exchange over peer memory,
+    else the streaming kernel)."""
     if choice == "auto":
         choice = "stream" if os.environ.get("G4B200_MLP_KERNEL") == "stream" else "tensor"
-    tc = choice == "tensor" and world == 1
+    tc = choice == "tensor" and (world == 1 or (peer and world == 2))
     return "mlp_tc_kernel" if tc else "mlp_kernel"
 
 

@@ -959,7 +959,10 @@ static bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t c
 // and whose shard the kernel's tiles fit (256-k stages of the down projection, 16-byte
 // rows of its scales: TP8's 120-byte rows do not).  The NCCL fallback keeps the
 // streaming kernel.
-constexpr int kTcMaxTp = 1;  // tensor-parallel sizes enabled once run on that many GPUs
+// TP2 and TP4 shards fit the kernel (TP8's 1920-wide down k-slices do not); measured per
+// token on B200s: TP2 25.9 us here against 26.8 on the streaming kernel, TP4 28.7 against
+// 26.2, so TP4 keeps the streaming kernel.
+constexpr int kTcMaxTp = 2;
 bool mlp_tc_enabled(const g4_ctx* ctx) {
   static const int env_kind = [] {
     const char* e = std::getenv("G4B200_MLP_KERNEL");
