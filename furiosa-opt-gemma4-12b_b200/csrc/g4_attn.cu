@@ -637,39 +637,86 @@ __global__ void __launch_bounds__(kFaMergeThreads) fa_merge_kernel(const float* 
 }
 
 // ---------------------------------------------------------------------------- sliding, clustered
-// The 1024-slot ring of one KV head in ONE cluster of 8 CTAs: CTA r copies slots
-// [128 r, 128 r + 128) of K and V into shared memory as 16 TMA boxes each (the cache
-// viewed as [slot][kv head][256]: box 8 slots x 1 head x 256), computes its partial
-// softmax statistics and weighted V sum for the head's 2 q heads, and the cluster merges
-// the 8 partials through distributed shared memory: CTA r stores dims [32 c, 32 c + 32)
-// of its partial into CTA c's shared memory, one cluster barrier, and CTA c adds the 8
-// partials of its dims in CTA order -- no global round trip, no counter.
+// The 1024-slot ring of one KV head in ONE cluster of 8 CTAs.  CTA r copies slots
+// [128 r, 128 r + 128) of K and V into shared memory with TMA (the cache viewed as
+// [slot][kv head][256]; box 64 dims x 1 head x 128 slots with the 128-byte swizzle, so each
+// tensor lands as 4 dim blocks [128 slots][64 dims] in the layout the tensor cores read),
+// and both contractions run on the 5th-generation tensor cores (tcgen05.mma .kind::f16,
+// bf16 x bf16 -> f32 in tensor memory, issued by one thread):
+//   scores  S^T[128 slots][16] = K[128 slots][256] . Q^T, A = the K blocks (K-major),
+//           B = the 2 q heads in rows 0-1 of a 16-row tile (the rest zero);
+//   values  O^T[128 dims][16] = V^T[128 dims][128 slots] . P^T (twice: dims 0-127 and
+//           128-255), A = the V blocks read dims-contiguous (MN-major: 64-dim rows of 8
+//           slots per 1 KB atom, the next 8 slots 1 KB on, the next 64 dims 16 KB on),
+//           B = P in rows 0-1 (bf16) and its remainders P - bf16(P) in rows 2-3 (bf16), so
+//           O = column h + column 2 + h carries about 16 significant bits of P.
+// Softmax in f32 as the reference (scripts/generate_references.py:324-330), masked slots
+// at -inf; V rows of masked slots are zeroed first (unused ring slots may hold anything,
+// and 0 * NaN is NaN).  The cluster merges the 8 partials through distributed shared
+// memory: CTA r stores dims [32 c, 32 c + 32) of its partial into CTA c's shared memory,
+// one cluster barrier, and CTA c adds the 8 partials of its dims in CTA order.
 // The copies start before griddepcontrol.wait.  A ring slot is rewritten only by the
-// attention projection of the same layer: when the launch knows that projection's
-// device offset (`fresh`, its kv_off), the CTA holding that slot copies its K and V rows
-// again after the wait; every other slot was written by kernels that completed before
-// this launch could start.  Same math as sliding_attn_kernel with 128-slot chunks.
+// attention projection of the same layer: when the launch knows that projection's device
+// offset (`fresh`, its kv_off), the CTA holding that slot copies its K and V rows again
+// after the wait; every other slot was written by kernels that completed before this
+// launch could start.
 constexpr int kScRows = 128;
 constexpr int kScCtas = TS / kScRows;  // 8: the cluster
-constexpr int kScThreads = 512;
-constexpr int kScWarps = kScThreads / 32;
-constexpr int kScRpw = kScRows / kScWarps;  // slots per warp: 8
-static_assert(GS * kScRpw == 16, "the scores' butterfly sums 16 values per lane");
-static_assert(GS * DS == kScThreads, "one output per thread in the cross-warp sum");
-constexpr int kScBox = kScRows / 16;   // slots per TMA box
+constexpr int kScThreads = 256;
+constexpr int kScBox = kScRows;        // slots per TMA box: a whole dim block in one copy
+constexpr int kScDimBlk = 64;          // dims per TMA box (128 bytes: the swizzle span)
+constexpr uint32_t kScCols = 64;       // tensor memory: S [0,16), O dims 0-127 [16,32), 128-255 [32,48)
+static_assert(GS == 2, "two q heads per KV head");
+// kind::f16: D f32, A and B bf16, N = 16, M = 128; A K-major (scores) or MN-major (values)
+constexpr uint32_t kScIdescK = (1u << 4) | (1u << 7) | (1u << 10) | (2u << 17) | (8u << 24);
+constexpr uint32_t kScIdescMN = kScIdescK | (1u << 15);
 
-struct __align__(128) ScSmem {  // TMA destinations: 128-byte aligned
-  uint16_t k[kScRows][DS];
-  uint16_t v[kScRows][DS];
-  float red[kScWarps][GS][DS];
-  float q[GS][DS];
+struct __align__(1024) ScSmem {  // 128-byte-swizzled operands: 1024-byte aligned
+  uint16_t k[DS / kScDimBlk][kScRows][kScDimBlk];  // 64 KB
+  uint16_t v[DS / kScDimBlk][kScRows][kScDimBlk];  // 64 KB
+  uint16_t qb[DS / kScDimBlk][16][kScDimBlk];      // B of the scores: [dim block][16 rows][64]
+  uint16_t pb[kScRows / 64][16][64];               // B of the values: [slot block][16 rows][64]
   float mo[kScCtas][GS][32];  // partial weighted sums of this CTA's 32 dims, from CTA c
   float mm[kScCtas][GS], ml[kScCtas][GS];  // and CTA c's softmax max / sum
   float s[GS][kScRows];
   float valid[kScRows];
   float m[GS], l[GS];
-  uint64_t full;
+  uint64_t full, sdone, odone;
+  uint32_t tmem;
 };
+// Byte offset of 8-element chunk c (elements 8c .. 8c + 7) of row `row` in a 128-byte
+// swizzled block of 128-byte rows.
+__device__ __forceinline__ uint32_t sw128_off(int row, int c) {
+  return static_cast<uint32_t>(row * 128 + (((c & 7) ^ (row & 7)) << 4));
+}
+// Shared-memory matrix descriptor, 128-byte swizzle: leading / stride byte offsets in bytes.
+__device__ __forceinline__ uint64_t sc_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+         (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (static_cast<uint64_t>(1u) << 46) |
+         (static_cast<uint64_t>(2u) << 61);
+}
+__device__ __forceinline__ void sc_mma(uint32_t d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(da), "l"(db), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void sc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void sc_ld4(uint32_t taddr, float (&v)[4]) {
+  uint32_t r[4];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void sc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void sc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -709,32 +756,57 @@ __global__ void __launch_bounds__(kScThreads) sliding_attn_cluster_kernel(const 
                                                                           uint64_t budget_ns, const uint16_t* kc,
                                                                           const uint16_t* vc, const int32_t* fresh) {
   extern __shared__ uint8_t sc_raw[];
-  ScSmem& sm = *reinterpret_cast<ScSmem*>((reinterpret_cast<uintptr_t>(sc_raw) + 127) & ~uintptr_t(127));
+  ScSmem& sm = *reinterpret_cast<ScSmem*>((reinterpret_cast<uintptr_t>(sc_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t r = cluster_ctarank();
   const int h = blockIdx.x / kScCtas;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int row0 = static_cast<int>(r) * kScRows;
   if (tid == 0) {
     mbar_init(&sm.full, 1);
+    mbar_init(&sm.sdone, 1);
+    mbar_init(&sm.odone, 1);
     fence_mbar_init();
   }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm.tmem)),
+                 "r"(kScCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+  }
+  // B tiles: every row but the ones written below is zero (q rows 0-1; P rows 0-3)
+  for (int i = tid; i < (DS / kScDimBlk) * 16 * 8; i += kScThreads) {
+    const int row = (i >> 3) & 15;
+    if (row >= GS) reinterpret_cast<uint4*>(&sm.qb[0][0][0])[i] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  for (int i = tid; i < (kScRows / 64) * 16 * 8; i += kScThreads) {
+    const int row = (i >> 3) & 15;
+    if (row >= 2 * GS) reinterpret_cast<uint4*>(&sm.pb[0][0][0])[i] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  sc_fence_before();
   __syncthreads();
+  sc_fence_after();
+  const uint32_t tbase = sm.tmem;
   cluster_arrive_relaxed();  // waited for before the first store into another CTA
   if (warp == 0) {
-    // 16 boxes of 8 slots per tensor, one per lane: many copies in flight at once
+    // one 16 KB box per dim block and tensor: lanes 0-3 K, 4-7 V
     const uint64_t pol = l2_evict_first_policy();  // 335 MB of rings per token: streamed
     if (lane == 0) mbar_arrive_expect_tx(&sm.full, 2u * kScRows * DS * 2u);
     __syncwarp();
-    const int b = lane & 15;
-    if (lane < 16)
-      tma_3d_load(sm.k[kScBox * b], &kmap, 0, h, row0 + kScBox * b, &sm.full, pol);
-    else
-      tma_3d_load(sm.v[kScBox * b], &vmap, 0, h, row0 + kScBox * b, &sm.full, pol);
+    if (lane < 2 * (DS / kScDimBlk)) {
+      const int b = lane % (DS / kScDimBlk);
+      const bool is_k = lane < DS / kScDimBlk;
+      tma_3d_load(is_k ? &sm.k[b][0][0] : &sm.v[b][0][0], is_k ? &kmap : &vmap, kScDimBlk * b, h, row0, &sm.full,
+                  pol);
+    }
   }
   pdl_wait();  // q, the mask and the newest cache row come from earlier kernels
   const uint64_t deadline = global_ns() + budget_ns;
-  for (int i = tid; i < GS * DS; i += kScThreads)
-    sm.q[i / DS][i % DS] = bf16_to_f32(q[static_cast<size_t>(h) * GS * DS + i]);
+  uint8_t* kbase = reinterpret_cast<uint8_t*>(&sm.k[0][0][0]);
+  uint8_t* vbase = reinterpret_cast<uint8_t*>(&sm.v[0][0][0]);
+  if (tid < GS * DS / 8) {  // q: head tid / 32, dims 8 (tid % 32) .. +7 into rows 0-1 of its dim block
+    const int hh = tid >> 5, c = tid & 31;
+    const uint4 w = reinterpret_cast<const uint4*>(q + static_cast<size_t>(h) * GS * DS)[tid];
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(&sm.qb[c >> 3][0][0]) + sw128_off(hh, c)) = w;
+  }
   if (tid < kScRows) sm.valid[tid] = mask[row0 + tid];
   const int nkv = static_cast<int>(gridDim.x) / kScCtas;
   int fslot = -1;  // the slot the projection just wrote, when this CTA holds it
@@ -745,119 +817,124 @@ __global__ void __launch_bounds__(kScThreads) sliding_attn_cluster_kernel(const 
   }
   if (!mbar_wait(&sm.full, 0u, deadline)) atomicOr(&scr->status, DEV_ERR_TIMEOUT_MBAR);
   if (fslot >= 0 && tid < 64) {  // after the boxes landed: these stores come last
-    const size_t src = (static_cast<size_t>(fslot) * nkv + h) * DS + 8 * (tid & 31);
+    const int c = tid & 31, row = fslot - row0;
+    const size_t src = (static_cast<size_t>(fslot) * nkv + h) * DS + 8 * c;
     const uint4 w = *reinterpret_cast<const uint4*>((tid < 32 ? kc : vc) + src);
-    *reinterpret_cast<uint4*>(tid < 32 ? &sm.k[fslot - row0][8 * (tid & 31)] : &sm.v[fslot - row0][8 * (tid & 31)]) = w;
+    uint8_t* blk = (tid < 32 ? kbase : vbase) + (c >> 3) * (kScRows * 128);
+    *reinterpret_cast<uint4*>(blk + sw128_off(row, c)) = w;
   }
-  __syncthreads();
+  fence_proxy_async();  // the generic-proxy writes above (q, the new row) are read by the tensor cores
+  // the mask is in; masked slots' V rows go to zero (P is 0 there, and 0 * whatever an
+  // unused slot holds must be 0) -- only a ring that is not yet full has any
+  if (__syncthreads_or(tid < kScRows && !(sm.valid[tid] > 0.f))) {
+    for (int i = tid; i < kScRows * (DS / 8); i += kScThreads) {
+      const int slot = i >> 5, c = i & 31;
+      if (!(sm.valid[slot] > 0.f))
+        *reinterpret_cast<uint4*>(vbase + (c >> 3) * (kScRows * 128) + sw128_off(slot, c)) =
+            make_uint4(0u, 0u, 0u, 0u);
+    }
+    fence_proxy_async();
+    __syncthreads();
+  }
   pdl_launch_dependents();
-  // scores: warp w owns slots 8 w .. 8 w + 7, lane l dims 8 l .. 8 l + 7; a lane's 16
-  // partial dot products (2 q heads x 8 slots) are summed over the warp by a butterfly
-  // that halves the values held per step (16 shuffles instead of 16 x 5): lane l ends
-  // with the sum of value l % 16 (q head (l % 16) / 8, slot 8 w + l % 8)
-  {
-    float qa[8], qb[8];
+  // ---- scores: 16 MMAs of K = 16 dims (4 per 64-dim block: +32 bytes in the swizzled row)
+  if (tid == 0) {
+    sc_fence_after();
+    const uint32_t kb = smem_u32(kbase), qb = smem_u32(&sm.qb[0][0][0]);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      qa[i] = sm.q[0][8 * lane + i];
-      qb[i] = sm.q[1][8 * lane + i];
+    for (int b = 0; b < DS / kScDimBlk; ++b)
+#pragma unroll
+      for (int st = 0; st < 4; ++st)
+        sc_mma(tbase, sc_desc(kb + b * (kScRows * 128) + 32 * st, 16, 1024),
+               sc_desc(qb + b * (16 * 128) + 32 * st, 16, 1024), kScIdescK, (b | st) ? 1u : 0u);
+    sc_commit(&sm.sdone);
+  }
+  // ---- softmax in warps 0-3 straight from tensor memory (warp w: slots 32 w + lane), then
+  // P and its remainder into the values' B tile
+  if (warp < 4) {
+    const bool ok = mbar_wait(&sm.sdone, 0u, deadline, true);
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    if (ok) {
+      sc_fence_after();
+      sc_ld4(tbase + (static_cast<uint32_t>(32 * warp) << 16), d);
+    } else if (lane == 0) {
+      atomicOr(&scr->status, DEV_ERR_TIMEOUT_MBAR);
     }
-    float v[16];
+    const int slot = 32 * warp + lane;
+    const bool v = sm.valid[slot] > 0.f;
+    float sv[GS], mx[GS], e[GS], l[GS];
 #pragma unroll
-    for (int j = 0; j < kScRpw; ++j) {
-      float kf[8];
-      bf16x8_to_f32(*reinterpret_cast<const uint4*>(&sm.k[kScRpw * warp + j][8 * lane]), kf);
-      float d0 = 0.f, d1 = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        d0 = fmaf(qa[i], kf[i], d0);
-        d1 = fmaf(qb[i], kf[i], d1);
-      }
-      v[j] = d0;
-      v[8 + j] = d1;
+    for (int hh = 0; hh < GS; ++hh) {
+      sv[hh] = v ? d[hh] : -CUDART_INF_F;
+      const float wm = warp_max(sv[hh]);
+      if (lane == 0) sm.s[hh][warp] = wm;  // s[][0..3]: per-warp maxima, then sums
     }
+    named_bar_sync(1, 128);
 #pragma unroll
-    for (int off = 8; off >= 1; off >>= 1) {
-      const bool up = (lane & off) != 0;
-#pragma unroll
-      for (int k = 0; k < off; ++k) {
-        const float send = up ? v[k] : v[k + off];
-        const float keep = up ? v[k + off] : v[k];
-        v[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-      }
+    for (int hh = 0; hh < GS; ++hh) {
+      mx[hh] = fmaxf(fmaxf(sm.s[hh][0], sm.s[hh][1]), fmaxf(sm.s[hh][2], sm.s[hh][3]));
+      e[hh] = (sv[hh] == -CUDART_INF_F) ? 0.f : expf(sv[hh] - mx[hh]);
+      l[hh] = warp_sum(e[hh]);
     }
-    v[0] += __shfl_xor_sync(0xffffffffu, v[0], 16);
-    if (lane < 16) {
-      const int hh = lane >> 3, row = kScRpw * warp + (lane & 7);
-      sm.s[hh][row] = sm.valid[row] > 0.f ? v[0] : -CUDART_INF_F;
+    if (lane == 0) {  // (sums go to s[][4..7], beside the maxima)
+      sm.s[0][4 + warp] = l[0];
+      sm.s[1][4 + warp] = l[1];
+    }
+    // P: rows 0-1 bf16, rows 2-3 the remainders; slot `slot` is element slot % 64 of block slot / 64
+    uint8_t* blk = reinterpret_cast<uint8_t*>(&sm.pb[slot >> 6][0][0]);
+    const int c = (slot & 63) >> 3, eb = (slot & 7) * 2;
+#pragma unroll
+    for (int hh = 0; hh < GS; ++hh) {
+      const float x = round_bf16(e[hh]);
+      *reinterpret_cast<uint16_t*>(blk + sw128_off(hh, c) + eb) = f32_to_bf16(x);
+      *reinterpret_cast<uint16_t*>(blk + sw128_off(GS + hh, c) + eb) = f32_to_bf16(e[hh] - x);
+    }
+    named_bar_sync(1, 128);
+    if (tid < GS) {
+      sm.m[tid] = mx[tid];
+      sm.l[tid] = ((sm.s[tid][4] + sm.s[tid][5]) + sm.s[tid][6]) + sm.s[tid][7];
     }
   }
+  fence_proxy_async();
   __syncthreads();
-  if (warp < GS) {
-    float e[4], mx = -CUDART_INF_F;
+  // ---- values: per dim half, 8 MMAs of K = 16 slots (the 8-slot atoms are 1 KB apart)
+  if (tid == 0) {
+    sc_fence_after();
+    const uint32_t vb = smem_u32(vbase), pb = smem_u32(&sm.pb[0][0][0]);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) mx = fmaxf(mx, sm.s[warp][lane + 32 * i]);
-    mx = warp_max(mx);
-    float l = 0.f;
+    for (int half = 0; half < 2; ++half)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float a = sm.s[warp][lane + 32 * i];
-      e[i] = (a == -CUDART_INF_F) ? 0.f : expf(a - mx);
-      l += e[i];
-    }
-    l = warp_sum(l);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) sm.s[warp][lane + 32 * i] = e[i];
-    if (lane == 0) {
-      sm.m[warp] = mx;
-      sm.l[warp] = l;
-    }
+      for (int j = 0; j < kScRows / 16; ++j)
+        sc_mma(tbase + 16u + 16u * half,
+               sc_desc(vb + half * 2 * (kScRows * 128) + j * 2048, kScRows * 128, 1024),
+               sc_desc(pb + (j >> 2) * (16 * 128) + 32 * (j & 3), 16, 1024), kScIdescMN, j ? 1u : 0u);
+    sc_commit(&sm.odone);
   }
-  __syncthreads();
-  // weighted V sum: warp w its 8 slots, lane l dims 8 l .. 8 l + 7, then the 16 warps'
-  // sums added in warp order
-  {
-    float o0[8], o1[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) o0[i] = o1[i] = 0.f;
-#pragma unroll
-    for (int j = 0; j < kScRpw; ++j) {
-      const int row = kScRpw * warp + j;
-      if (sm.valid[row] > 0.f) {  // unused ring slots may hold anything: never touched
-        float vf[8];
-        bf16x8_to_f32(*reinterpret_cast<const uint4*>(&sm.v[row][8 * lane]), vf);
-        const float p0 = sm.s[0][row], p1 = sm.s[1][row];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          o0[i] = fmaf(p0, vf[i], o0[i]);
-          o1[i] = fmaf(p1, vf[i], o1[i]);
-        }
-      }
-    }
-    float4* r0 = reinterpret_cast<float4*>(&sm.red[warp][0][8 * lane]);
-    float4* r1 = reinterpret_cast<float4*>(&sm.red[warp][1][8 * lane]);
-    r0[0] = make_float4(o0[0], o0[1], o0[2], o0[3]);
-    r0[1] = make_float4(o0[4], o0[5], o0[6], o0[7]);
-    r1[0] = make_float4(o1[0], o1[1], o1[2], o1[3]);
-    r1[1] = make_float4(o1[4], o1[5], o1[6], o1[7]);
-  }
-  __syncthreads();
   cluster_wait();  // every CTA of the cluster is running: its shared memory may be written
-  {
-    const int o = tid;  // GS * DS == kScThreads outputs, one per thread
-    const int hh = o / DS, d = o % DS;
-    float acc = 0.f;
+  if (warp < 4) {  // TMEM lane quarter `warp`: dims 128 half + 32 warp + lane
+    const bool ok = mbar_wait(&sm.odone, 0u, deadline, true);
+    if (!ok && lane == 0) atomicOr(&scr->status, DEV_ERR_TIMEOUT_MBAR);
 #pragma unroll
-    for (int w = 0; w < kScWarps; ++w) acc += sm.red[w][hh][d];
-    st_cluster_f32(&sm.mo[r][hh][d % 32], static_cast<uint32_t>(d / 32), acc);  // to the CTA finishing dim d
-    if (tid < GS * kScCtas) {
-      const int gh = tid / kScCtas, c = tid % kScCtas;
-      st_cluster_f32(&sm.mm[r][gh], static_cast<uint32_t>(c), sm.m[gh]);
-      st_cluster_f32(&sm.ml[r][gh], static_cast<uint32_t>(c), sm.l[gh]);
+    for (int half = 0; half < 2; ++half) {
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      if (ok) {
+        sc_fence_after();
+        sc_ld4(tbase + 16u + 16u * half + (static_cast<uint32_t>(32 * warp) << 16), d);
+      }
+      const int dim = 128 * half + 32 * warp + lane;
+      const uint32_t dst = static_cast<uint32_t>(dim >> 5);
+      st_cluster_f32(&sm.mo[r][0][dim & 31], dst, d[0] + d[2]);
+      st_cluster_f32(&sm.mo[r][1][dim & 31], dst, d[1] + d[3]);
     }
+  }
+  if (tid < GS * kScCtas) {
+    const int gh = tid / kScCtas, c = tid % kScCtas;
+    st_cluster_f32(&sm.mm[r][gh], static_cast<uint32_t>(c), sm.m[gh]);
+    st_cluster_f32(&sm.ml[r][gh], static_cast<uint32_t>(c), sm.l[gh]);
   }
   // Every CTA's partials are in place; after this barrier a CTA reads only its own shared
   // memory, so it may exit as soon as it is done.
+  sc_fence_before();
   cluster_arrive_release();
   cluster_wait_acquire();
   if (tid < GS * 32) {
@@ -878,6 +955,10 @@ __global__ void __launch_bounds__(kScThreads) sliding_attn_cluster_kernel(const 
       acc += w * oc[c];
     }
     out[(static_cast<size_t>(h) * GS + hh) * DS + d] = f32_to_bf16(ls > 0.f ? acc / ls : 0.f);
+  }
+  if (warp == 2) {  // every tensor-memory read of this CTA completed before the cluster barrier
+    sc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(kScCols));
   }
 }
 
@@ -913,7 +994,8 @@ using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, voi
                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                               CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 // The sliding cache [Ts][nkv][Ds] bf16 as a 3-D tensor (dims: Ds, nkv, Ts), box
-// 256 x 1 x 8: 8 slots of one head (a CTA's 128 slots are 16 boxes).
+// 64 x 1 x 128 (64 dims of a CTA's 128 slots of one head: 128-byte rows, 16 KB) with the
+// 128-byte swizzle.
 static bool cache_map(CUtensorMap* m, const void* base, int nkv) {
   static EncodeFn fn = [] {
     void* p = nullptr;
@@ -926,10 +1008,10 @@ static bool cache_map(CUtensorMap* m, const void* base, int nkv) {
   if (fn == nullptr || !aligned16(base)) return false;
   const cuuint64_t dims[3] = {DS, static_cast<cuuint64_t>(nkv), TS};
   const cuuint64_t strides[2] = {DS * 2, static_cast<cuuint64_t>(nkv) * DS * 2};
-  const cuuint32_t box[3] = {DS, 1, kScBox};
+  const cuuint32_t box[3] = {kScDimBlk, 1, kScBox};
   const cuuint32_t estr[3] = {1, 1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -943,7 +1025,7 @@ g4_status launch_sliding_attention(g4_ctx* ctx, const uint16_t* q, const uint16_
   const int nkv = NS / ctx->tp_world;
   if (ctx->cluster_ok && cache_map(&km, k, nkv) && cache_map(&vm, v, nkv)) {
     const void* fn = reinterpret_cast<const void*>(&sliding_attn_cluster_kernel);
-    const size_t smem = sizeof(ScSmem) + 128;
+    const size_t smem = sizeof(ScSmem) + 1024;
     g4_status st = allow_max_dynamic_smem(ctx, fn, smem, "sliding attention");
     if (st != G4_OK) return st;
     Scratch* scr = ctx->buf.scratch;
