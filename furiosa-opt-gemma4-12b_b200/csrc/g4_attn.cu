@@ -433,11 +433,35 @@ __global__ void __launch_bounds__(kFaThreads) fa_partial_kernel(const uint16_t* 
   extern __shared__ __align__(128) uint8_t fa_raw[];
   FaSmem& sm = *reinterpret_cast<FaSmem*>(fa_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  // tile loads: rows [tr, tr + 32) below `lim` into buffer b, one cp.async group per tile
+  auto load_tile_lim = [&](int tr, int b, int lim) {
+    const uint32_t kbb = smem_u32(sm.k[b]), vbb = smem_u32(sm.v[b]);
+    for (int i = tid; i < kFaTile * (DF / 8); i += kFaThreads) {
+      const int rr = i / (DF / 8), c = i % (DF / 8);
+      const int r = tr + rr;
+      const bool ok = r < lim;
+      const uint32_t off = rr * (DF * 2) + ((c ^ (rr & 7)) * 16);
+      cp_async16(kbb + off, ok ? fa_row(src, false, r) + c * 8 : q, ok ? 16u : 0u);
+      cp_async16(vbb + off, ok ? fa_row(src, true, r) + c * 8 : q, ok ? 16u : 0u);
+    }
+    cp_async_commit();
+  };
+  // When the grid covers max_rows in 64-row ranges (the launchers size it so), every row
+  // count gives this CTA rows [64 c, 64 c + 64): both tiles are copied before the wait.
+  // Rows below max_rows exist; all but the newest were written by kernels that completed
+  // before this launch could start, and the newest (row n - 1, the projection's) is copied
+  // again after the wait.
+  const bool early = static_cast<long long>(gridDim.x) * 2 * kFaTile >= src.max_rows;
+  if (early) {
+    load_tile_lim(blockIdx.x * 2 * kFaTile, 0, src.max_rows);
+    load_tile_lim(blockIdx.x * 2 * kFaTile + kFaTile, 1, src.max_rows);
+  }
   pdl_wait();  // q and the newest K/V row come from the projection kernel
   int n, rpc, nact;
   fa_split(src, gridDim.x, n, rpc, nact);
   const int r0 = blockIdx.x * rpc, r1 = min(n, r0 + rpc);
   if (r0 >= r1) {
+    cp_async_wait_all();  // no copy may still be landing in shared memory at exit
     pdl_launch_dependents();
     return;
   }
@@ -447,21 +471,30 @@ __global__ void __launch_bounds__(kFaThreads) fa_partial_kernel(const uint16_t* 
     const bool ok = hh < nq;
     cp_async16(qb + hh * kFaQStride + c * 16, ok ? q + hh * DF + c * 8 : q, ok ? 16u : 0u);
   }
-  // tile loads: rows [tr, tr + 32) into buffer b, one cp.async group per tile
-  auto load_tile = [&](int tr, int b) {
-    const uint32_t kbb = smem_u32(sm.k[b]), vbb = smem_u32(sm.v[b]);
-    for (int i = tid; i < kFaTile * (DF / 8); i += kFaThreads) {
+  auto load_tile = [&](int tr, int b) { load_tile_lim(tr, b, r1); };
+  if (!early) {
+    load_tile(r0, 0);
+    if (r0 + kFaTile < r1) load_tile(r0 + kFaTile, 1);
+  } else {
+    cp_async_commit();  // q
+    cp_async_wait_all();
+    __syncthreads();  // every early copy landed: the rows below can be rewritten
+    const int nr = n - 1 - r0;  // the newest row, when this CTA holds it
+    const uint32_t zero_from = static_cast<uint32_t>(r1 - r0);  // rows >= n: V to zero (may be stale)
+    for (int i = tid; i < 2 * kFaTile * (DF / 8); i += kFaThreads) {
       const int rr = i / (DF / 8), c = i % (DF / 8);
-      const int r = tr + rr;
-      const bool ok = r < r1;
-      const uint32_t off = rr * (DF * 2) + ((c ^ (rr & 7)) * 16);
-      cp_async16(kbb + off, ok ? fa_row(src, false, r) + c * 8 : q, ok ? 16u : 0u);
-      cp_async16(vbb + off, ok ? fa_row(src, true, r) + c * 8 : q, ok ? 16u : 0u);
+      const uint32_t off = (rr % kFaTile) * (DF * 2) + ((c ^ (rr & 7)) * 16);
+      const int b = rr / kFaTile;
+      if (rr == nr) {
+        cp_async16(smem_u32(sm.k[b]) + off, fa_row(src, false, r0 + rr) + c * 8, 16u);
+        cp_async16(smem_u32(sm.v[b]) + off, fa_row(src, true, r0 + rr) + c * 8, 16u);
+      } else if (static_cast<uint32_t>(rr) >= zero_from) {
+        *reinterpret_cast<uint4*>(sm.v[b] + off) = make_uint4(0u, 0u, 0u, 0u);
+      }
     }
     cp_async_commit();
-  };
-  load_tile(r0, 0);
-  if (r0 + kFaTile < r1) load_tile(r0 + kFaTile, 1);
+    cp_async_wait_all();
+  }
   if (tid < GF) {
     sm.m[tid] = -CUDART_INF_F;
     sm.l[tid] = 0.f;
@@ -583,6 +616,7 @@ __global__ void __launch_bounds__(kFaMergeThreads) fa_merge_kernel(const float* 
   __shared__ float osum[kFaMergeGroups][128];
   __shared__ float Mall, Lall;
   const int h = blockIdx.x >> 2, quarter = blockIdx.x & 3, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_launch_dependents();  // the attention output projection may start streaming its weights
   pdl_wait();  // every partial of the previous kernel is written
   int n, rpc, nact;
   fa_split(src, grid, n, rpc, nact);
