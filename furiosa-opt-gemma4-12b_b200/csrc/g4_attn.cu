@@ -996,6 +996,228 @@ __global__ void __launch_bounds__(kScThreads) sliding_attn_cluster_kernel(const 
   }
 }
 
+// ---------------------------------------------------------------------------- full (MQA), tcgen05
+// fa_partial_kernel's work on the 5th-generation tensor cores, for launches whose grid
+// covers max_rows in 64-row ranges (then CTA c holds rows [64 c, 64 c + 64) for every row
+// count).  The rows are copied before griddepcontrol.wait (16-byte cp.async chunks into
+// 128-byte-swizzled blocks [8 dim blocks][64 rows][64 dims]); after it the newest row is
+// copied again and V rows past the count are zeroed.  Then, with one issuing thread:
+//   scores S^T[rows][16 heads] = K . Q^T  (kind::f16, M = 128: rows 64-127 of each
+//          descriptor read the next block and are ignored; N = 16, 32 MMAs of 16 dims);
+//   softmax over the CTA's 64 rows in f32 (4 warps, 4 heads each);
+//   values O^T[128 dims][32] = V^T . [P; P - bf16(P)]^T for each quarter of the 512 dims
+//          (A = V read MN-major, B = 16 rows of P and 16 of its remainders, N = 32).
+// The CTA's (m, l, o[16][512]) partial goes to the same slot fa_merge_kernel reads.
+constexpr int kFtThreads = 128;
+constexpr int kFtRows = 64;
+constexpr uint32_t kFtCols = 256;  // S [0,16), O quarter j at [16 + 32 j, 48 + 32 j)
+constexpr uint32_t kFtIdescS = (1u << 4) | (1u << 7) | (1u << 10) | (2u << 17) | (8u << 24);
+constexpr uint32_t kFtIdescO = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (4u << 17) | (8u << 24);
+
+struct __align__(1024) FtSmem {
+  uint16_t k[DF / 64][kFtRows][64];  // 64 KB
+  uint16_t v[DF / 64][kFtRows][64];  // 64 KB (K's M = 128 descriptors read into here: ignored rows)
+  uint16_t qb[DF / 64][GF][64];      // 16 KB
+  uint16_t pb[2 * GF][kFtRows];      // 4 KB: P rows 0-15, remainders 16-31
+  float s[GF][kFtRows];
+  float m[GF], l[GF];
+  uint64_t sdone, odone;
+  uint32_t tmem;
+};
+
+__device__ __forceinline__ void ft_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void ft_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__global__ void __launch_bounds__(kFtThreads) fa_tc_kernel(const uint16_t* q, int nq, FaSrc src, float* part,
+                                                           Scratch* scr, uint64_t budget_ns) {
+  extern __shared__ uint8_t ft_raw[];
+  FtSmem& sm = *reinterpret_cast<FtSmem*>((reinterpret_cast<uintptr_t>(ft_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r0 = blockIdx.x * kFtRows;
+  uint8_t* kbase = reinterpret_cast<uint8_t*>(&sm.k[0][0][0]);
+  uint8_t* vbase = reinterpret_cast<uint8_t*>(&sm.v[0][0][0]);
+  // chunk c (dims 8c .. 8c + 7) of row rr in a [8][64][64] swizzled operand
+  auto off = [](int rr, int c) -> uint32_t {
+    return static_cast<uint32_t>((c >> 3) * (kFtRows * 128) + rr * 128 + (((c & 7) ^ (rr & 7)) << 4));
+  };
+  if (tid == 0) {
+    mbar_init(&sm.sdone, 1);
+    mbar_init(&sm.odone, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm.tmem)),
+                 "r"(kFtCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+  }
+  for (int i = tid; i < kFtRows * (DF / 8); i += kFtThreads) {  // rows below max_rows, before the wait
+    const int rr = i / (DF / 8), c = i % (DF / 8), r = r0 + rr;
+    const bool ok = r < src.max_rows;
+    cp_async16(smem_u32(kbase) + off(rr, c), ok ? fa_row(src, false, r) + c * 8 : q, ok ? 16u : 0u);
+    cp_async16(smem_u32(vbase) + off(rr, c), ok ? fa_row(src, true, r) + c * 8 : q, ok ? 16u : 0u);
+  }
+  cp_async_commit();
+  sc_fence_before();
+  __syncthreads();
+  sc_fence_after();
+  const uint32_t tbase = sm.tmem;
+  pdl_wait();  // q and the newest K/V row come from the projection kernel
+  const uint64_t deadline = global_ns() + budget_ns;
+  int n, rpc, nact;
+  fa_split(src, gridDim.x, n, rpc, nact);
+  const int r1 = min(n, r0 + kFtRows);
+  if (r0 < r1) {
+    for (int i = tid; i < GF * (DF / 8); i += kFtThreads) {  // Q rows (heads past nq zero)
+      const int hh = i / (DF / 8), c = i % (DF / 8);
+      const bool ok = hh < nq;
+      cp_async16(smem_u32(&sm.qb[0][0][0]) + static_cast<uint32_t>((c >> 3) * (GF * 128) + hh * 128 +
+                                                                  (((c & 7) ^ (hh & 7)) << 4)),
+                 ok ? q + hh * DF + c * 8 : q, ok ? 16u : 0u);
+    }
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncthreads();  // every early copy landed: the newest row and the rows past n may be rewritten
+    const int nr = n - 1 - r0;
+    for (int i = tid; i < kFtRows * (DF / 8); i += kFtThreads) {
+      const int rr = i / (DF / 8), c = i % (DF / 8);
+      if (rr == nr) {
+        cp_async16(smem_u32(kbase) + off(rr, c), fa_row(src, false, r0 + rr) + c * 8, 16u);
+        cp_async16(smem_u32(vbase) + off(rr, c), fa_row(src, true, r0 + rr) + c * 8, 16u);
+      } else if (rr >= r1 - r0) {
+        *reinterpret_cast<uint4*>(vbase + off(rr, c)) = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    cp_async_commit();
+    cp_async_wait_all();
+  } else {
+    cp_async_wait_all();
+  }
+  fence_proxy_async();  // the copies and stores above are read by the tensor cores
+  __syncthreads();
+  pdl_launch_dependents();
+  if (r0 < r1) {
+    // ---- scores
+    if (tid == 0) {
+      sc_fence_after();
+      const uint32_t kb = smem_u32(kbase), qb = smem_u32(&sm.qb[0][0][0]);
+#pragma unroll
+      for (int b = 0; b < DF / 64; ++b)
+#pragma unroll
+        for (int st = 0; st < 4; ++st)
+          sc_mma(tbase, sc_desc(kb + b * (kFtRows * 128) + 32 * st, 16, 1024),
+                 sc_desc(qb + b * (GF * 128) + 32 * st, 16, 1024), kFtIdescS, (b | st) ? 1u : 0u);
+      sc_commit(&sm.sdone);
+    }
+    if (warp < 2) {  // rows 32 warp + lane (TMEM lanes 0-63)
+      const bool ok = mbar_wait(&sm.sdone, 0u, deadline, true);
+      float d[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) d[i] = 0.f;
+      if (ok) {
+        sc_fence_after();
+        ft_ld16(tbase + (static_cast<uint32_t>(32 * warp) << 16), d);
+      } else if (lane == 0) {
+        atomicOr(&scr->status, DEV_ERR_TIMEOUT_MBAR);
+      }
+      const int rr = 32 * warp + lane;
+      const bool v = r0 + rr < r1;
+#pragma unroll
+      for (int hh = 0; hh < GF; ++hh) sm.s[hh][rr] = v ? d[hh] : -CUDART_INF_F;
+    }
+    __syncthreads();
+    // ---- softmax: warp w heads 4w .. 4w + 3, lane rows lane and lane + 32
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int hh = 4 * warp + j;
+      const float a = sm.s[hh][lane], b = sm.s[hh][lane + 32];
+      const float mx = warp_max(fmaxf(a, b));
+      const float pa = (a == -CUDART_INF_F) ? 0.f : expf(a - mx);
+      const float pb = (b == -CUDART_INF_F) ? 0.f : expf(b - mx);
+      const float l = warp_sum(pa + pb);
+      if (lane == 0) {
+        sm.m[hh] = mx;
+        sm.l[hh] = l;
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int rr = lane + 32 * e;
+        const float p = e ? pb : pa, x = round_bf16(p);
+        uint8_t* row_hi = reinterpret_cast<uint8_t*>(&sm.pb[hh][0]);
+        uint8_t* row_lo = reinterpret_cast<uint8_t*>(&sm.pb[GF + hh][0]);
+        const uint32_t o_hi = (((rr >> 3) ^ (hh & 7)) << 4) + (rr & 7) * 2;
+        const uint32_t o_lo = (((rr >> 3) ^ ((GF + hh) & 7)) << 4) + (rr & 7) * 2;
+        *reinterpret_cast<uint16_t*>(row_hi + o_hi) = f32_to_bf16(x);
+        *reinterpret_cast<uint16_t*>(row_lo + o_lo) = f32_to_bf16(p - x);
+      }
+    }
+    fence_proxy_async();
+    __syncthreads();
+    // ---- values: dims quarter j (dim blocks 2j, 2j + 1), 4 MMAs of 16 rows each
+    if (tid == 0) {
+      sc_fence_after();
+      const uint32_t vb = smem_u32(vbase), pbb = smem_u32(&sm.pb[0][0]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int ks = 0; ks < kFtRows / 16; ++ks)
+          sc_mma(tbase + 16u + 32u * j, sc_desc(vb + 2 * j * (kFtRows * 128) + ks * 2048, kFtRows * 128, 1024),
+                 sc_desc(pbb + 32 * ks, 16, 1024), kFtIdescO, ks ? 1u : 0u);
+      sc_commit(&sm.odone);
+    }
+    float* mine = part + static_cast<size_t>(blockIdx.x) * kFaPart;
+    {
+      const bool ok = mbar_wait(&sm.odone, 0u, deadline, true);
+      if (!ok && lane == 0) atomicOr(&scr->status, DEV_ERR_TIMEOUT_MBAR);
+#pragma unroll 1
+      for (int j = 0; j < 4; ++j) {  // warp w: dims 128 j + 32 w + lane
+        float d[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) d[i] = 0.f;
+        if (ok) {
+          sc_fence_after();
+          ft_ld32(tbase + 16u + 32u * j + (static_cast<uint32_t>(32 * warp) << 16), d);
+        }
+        const int dim = 128 * j + 32 * warp + lane;
+#pragma unroll
+        for (int hh = 0; hh < GF; ++hh) mine[2 * GF + hh * DF + dim] = d[hh] + d[GF + hh];
+      }
+    }
+    if (tid < GF) {
+      mine[tid] = sm.m[tid];
+      mine[GF + tid] = sm.l[tid];
+    }
+  }
+  sc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(kFtCols));
+  }
+}
+
 // ---------------------------------------------------------------------------- launchers
 g4_status launch_full_page(g4_ctx* ctx, bool first, const uint16_t* q, const uint16_t* k, const uint16_t* v,
                            const float* mask, float* rmax, float* rsum, uint16_t* out) {
@@ -1083,13 +1305,25 @@ static g4_status launch_full_attention(g4_ctx* ctx, const uint16_t* q, const FaS
   int grid = 2 * ctx->sm_count;
   if (grid > kFaMaxCtas) grid = kFaMaxCtas;
   if (want < grid) grid = want < 1 ? 1 : want;
-  g4_status st = allow_max_dynamic_smem(ctx, (const void*)fa_partial_kernel, sizeof(FaSmem), "full attention");
-  if (st != G4_OK) return st;
   float* part = ctx->buf.attn;
   FaSrc s = src;
-  void* a1[] = {(void*)&q, (void*)&nq, (void*)&s, (void*)&part};
-  st = launch_kernel(ctx, (const void*)fa_partial_kernel, dim3(grid), dim3(kFaThreads), sizeof(FaSmem), a1, false,
-                     "full attention partials");
+  g4_status st;
+  if (static_cast<long long>(grid) * kFtRows >= src.max_rows) {  // 64 rows per CTA: the tensor-core kernel
+    const size_t smem = sizeof(FtSmem) + 1024;
+    st = allow_max_dynamic_smem(ctx, (const void*)fa_tc_kernel, smem, "full attention");
+    if (st != G4_OK) return st;
+    Scratch* scr = ctx->buf.scratch;
+    uint64_t budget = ctx->wait_budget_ns;
+    void* a1[] = {(void*)&q, (void*)&nq, (void*)&s, (void*)&part, (void*)&scr, (void*)&budget};
+    st = launch_kernel(ctx, (const void*)fa_tc_kernel, dim3(grid), dim3(kFtThreads), smem, a1, false,
+                       "full attention partials");
+  } else {
+    st = allow_max_dynamic_smem(ctx, (const void*)fa_partial_kernel, sizeof(FaSmem), "full attention");
+    if (st != G4_OK) return st;
+    void* a1[] = {(void*)&q, (void*)&nq, (void*)&s, (void*)&part};
+    st = launch_kernel(ctx, (const void*)fa_partial_kernel, dim3(grid), dim3(kFaThreads), sizeof(FaSmem), a1, false,
+                       "full attention partials");
+  }
   if (st != G4_OK) return st;
   void* a2[] = {(void*)&part, (void*)&s, (void*)&grid, (void*)&rsum, (void*)&out};
   return launch_kernel(ctx, (const void*)fa_merge_kernel, dim3(4 * nq), dim3(kFaMergeThreads), 0, a2, false,
