@@ -111,10 +111,11 @@ const char* g4_ctx_last_error(const g4_ctx* ctx);
  * bit in the context's device status word and its kernel returns early. */
 g4_status g4_ctx_set_wait_budget(g4_ctx* ctx, uint32_t timeout_us);
 /* Which kernel runs decoder_feedforward on this context (no reference counterpart):
- * G4_MLP_AUTO (the default; G4B200_MLP_KERNEL=stream|tc in the environment picks it) or
- * G4_MLP_TENSOR run the tcgen05 block-scaled FP4 kernel on one GPU; G4_MLP_STREAM
- * (CUDA-core NVFP4 decode + mma.sync) runs tensor-parallel contexts and can be asked
- * for anywhere.  Same results within f32 rounding of the dot products. */
+ * G4_MLP_AUTO (the default; G4B200_MLP_KERNEL=stream in the environment switches it) or
+ * G4_MLP_TENSOR run the tcgen05 block-scaled FP4 kernel on one GPU and on 2-GPU
+ * tensor-parallel contexts that exchange over peer memory; G4_MLP_STREAM (CUDA-core NVFP4
+ * decode + mma.sync) runs the other tensor-parallel contexts and can be asked for
+ * anywhere.  Same results within f32 rounding of the dot products. */
 enum { G4_MLP_AUTO = 0, G4_MLP_STREAM = 1, G4_MLP_TENSOR = 2 };
 g4_status g4_ctx_set_mlp_kernel(g4_ctx* ctx, int kind);
 
