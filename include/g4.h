@@ -30,6 +30,15 @@
  * aligned (cudaMalloc gives 256).  Shapes are the reference's fixed axes unless an
  * entry point says otherwise; under tensor parallelism (g4_ctx_init_tp) the weight
  * arguments are this rank's shard, as documented per entry point.
+ *
+ * Overlap between consecutive calls: kernels are launched with programmatic dependent
+ * launch, and before waiting for the previous kernel on the stream they read only data
+ * that kernel cannot be writing -- weights and norm weights, and (sliding and full
+ * attention) KV-cache rows other than the one the attention projection launched last on
+ * the context wrote, which they read again after the wait.  A kernel of the caller's own
+ * that precedes a g4 call on the same stream is waited for as usual unless it triggers
+ * programmatic completion early itself (griddepcontrol.launch_dependents), in which case
+ * it must not be writing weights or cache rows the next g4 call reads.
  */
 #ifndef G4_B200_API_H_
 #define G4_B200_API_H_
