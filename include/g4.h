@@ -33,9 +33,10 @@
  *
  * Overlap between consecutive calls: kernels are launched with programmatic dependent
  * launch, and before waiting for the previous kernel on the stream they read only data
- * that kernel cannot be writing -- weights and norm weights, and (sliding and full
- * attention) KV-cache rows other than the one the attention projection launched last on
- * the context wrote, which they read again after the wait.  A kernel of the caller's own
+ * that kernel cannot be writing -- weights and norm weights, and KV-cache rows other
+ * than the newest (sliding attention: the row the context's last attention projection
+ * wrote into that cache; full attention: the last row of the range), which they read again
+ * after the wait.  A kernel of the caller's own
  * that precedes a g4 call on the same stream is waited for as usual unless it triggers
  * programmatic completion early itself (griddepcontrol.launch_dependents), in which case
  * it must not be writing weights or cache rows the next g4 call reads.
